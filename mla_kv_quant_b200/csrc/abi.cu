@@ -1,0 +1,287 @@
+// extern "C" entry points of librolaq_b200.so (declared in include/rolaq_b200.h).
+// Every function validates its arguments on the host before launching, returns a
+// status code, and records a message for rolaq_last_error() on failure.
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+
+#include "kernels.cuh"
+
+namespace rolaq {
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+}  // namespace rolaq
+
+using namespace rolaq;
+
+namespace {
+
+thread_local char g_msg[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_cache(const rolaq_layer_cache* c, bool need_window, bool need_rope = true) {
+  if (c == nullptr) return fail(ROLAQ_EINVAL, "cache is NULL");
+  if (c->latent_dim != 256 && c->latent_dim != 512)
+    return fail(ROLAQ_EUNSUPPORTED, "latent_dim %d unsupported (256 or 512)", c->latent_dim);
+  if (need_rope && (c->rope_dim <= 0 || c->rope_dim % 16 != 0 || c->rope_dim > 128))
+    return fail(ROLAQ_EUNSUPPORTED, "rope_dim %d unsupported (multiple of 16, <= 128)", c->rope_dim);
+  if (!c->codes || !c->params || (need_rope && !c->rope))
+    return fail(ROLAQ_EINVAL, "cache codes/params/rope must be non-NULL");
+  if (!aligned16(c->codes) || !aligned16(c->params) || (need_rope && !aligned16(c->rope)))
+    return fail(ROLAQ_EINVAL, "cache codes/params/rope must be 16-byte aligned");
+  if (c->num_slots <= 0 || c->num_slots >= (int64_t(1) << 31))
+    return fail(ROLAQ_EINVAL, "num_slots %lld out of range", (long long)c->num_slots);
+  if (c->sink < 0 || c->recent < 0) return fail(ROLAQ_EINVAL, "sink/recent must be >= 0");
+  if (need_window && c->sink + c->recent > 0) {
+    if (!c->hp || !c->rows || !c->owners) return fail(ROLAQ_EINVAL, "window enabled but hp/rows/owners is NULL");
+    if (!aligned16(c->hp)) return fail(ROLAQ_EINVAL, "hp must be 16-byte aligned");
+    if (c->max_reqs < 0 || c->num_ring_rows < 1 + c->max_reqs * (c->sink + c->recent))
+      return fail(ROLAQ_EINVAL, "num_ring_rows %lld < 1 + max_reqs*(sink+recent)", (long long)c->num_ring_rows);
+  }
+  return ROLAQ_OK;
+}
+
+int codec_ok(const rolaq_codec& k) {
+  if (!(k.threshold > 0.f) || !(k.scale_factor > 0.f) || !(k.threshold < 1e30f) || !(k.scale_factor < 1e30f))
+    return fail(ROLAQ_EINVAL, "codec threshold and scale_factor must be finite and > 0");
+  return ROLAQ_OK;
+}
+
+int cuda_rc(int rc, const char* what) {
+  if (rc == ROLAQ_ECUDA) {
+    cudaError_t e = cudaGetLastError();
+    return fail(ROLAQ_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+  }
+  return rc;
+}
+
+}  // namespace
+
+extern "C" {
+
+int rolaq_version(void) { return 10000; }
+
+const char* rolaq_last_error(void) { return g_msg; }
+
+int rolaq_check_device(void) {
+  int dev = 0, major = 0, minor = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(ROLAQ_ECUDA, "no CUDA device");
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (major != 10 || minor != 0)
+    return fail(ROLAQ_EUNSUPPORTED, "device is sm_%d%d; this library is built for sm_100a only", major, minor);
+  if (encode_fn() == nullptr) return fail(ROLAQ_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  return ROLAQ_OK;
+}
+
+int rolaq_scatter_pack_rows(const float* x, int64_t ldx, const void* slots, int slots_are_int64, int64_t n,
+                            int32_t latent_dim, int32_t group_size, rolaq_codec codec, uint8_t* codes,
+                            float* params, int64_t num_slots, int32_t* err, cudaStream_t stream) {
+  if (n < 0) return fail(ROLAQ_EINVAL, "n < 0");
+  if (group_size != 128) return fail(ROLAQ_EUNSUPPORTED, "group_size %d unsupported (128)", group_size);
+  if (latent_dim <= 0 || latent_dim % 128) return fail(ROLAQ_EUNSUPPORTED, "latent_dim must be a multiple of 128");
+  if (n == 0) return ROLAQ_OK;
+  if (!x || !slots || !codes || !params) return fail(ROLAQ_EINVAL, "NULL pointer");
+  if (!aligned16(x) || ldx < latent_dim || ldx % 4) return fail(ROLAQ_EINVAL, "x must be 16-byte aligned, ldx >= D, ldx %% 4 == 0");
+  if (!aligned16(codes) || !aligned16(params)) return fail(ROLAQ_EINVAL, "codes/params must be 16-byte aligned");
+  if (int rc = codec_ok(codec)) return rc;
+  return cuda_rc(launch_scatter_pack(x, ldx, slots, slots_are_int64, n, latent_dim, codec, codes, params, num_slots,
+                                     err, stream),
+                 "scatter_pack");
+}
+
+int rolaq_write_aux(const float* c, int64_t ldc, const uint16_t* k_pe, int64_t ld_pe, const int64_t* slots,
+                    const void* seq_lens, int seq_lens_is64, const void* req_idx, int req_idx_is64,
+                    const void* positions, int positions_is64, int64_t n, const rolaq_layer_cache* cache,
+                    int32_t* err, cudaStream_t stream) {
+  if (n < 0) return fail(ROLAQ_EINVAL, "n < 0");
+  if (int rc = check_cache(cache, seq_lens != nullptr && req_idx != nullptr)) return rc;
+  if (n == 0) return ROLAQ_OK;
+  if (!c || !k_pe || !slots) return fail(ROLAQ_EINVAL, "NULL pointer");
+  if (ldc < cache->latent_dim || ld_pe < cache->rope_dim) return fail(ROLAQ_EINVAL, "row stride too small");
+  return cuda_rc(launch_aux(c, ldc, k_pe, ld_pe, slots, seq_lens, seq_lens_is64, req_idx, req_idx_is64, positions,
+                            positions_is64, n, *cache, err, stream),
+                 "write_aux");
+}
+
+int rolaq_fused_write(const uint16_t* c_kv, int64_t ld_ckv, const uint16_t* k_pe, int64_t ld_pe,
+                      const int64_t* slots, const void* seq_lens, int seq_lens_is64, const void* req_idx,
+                      int req_idx_is64, const void* positions, int positions_is64, int64_t n,
+                      const uint16_t* rot_t, rolaq_codec codec, const rolaq_layer_cache* cache, int32_t* err,
+                      cudaStream_t stream) {
+  if (n < 0) return fail(ROLAQ_EINVAL, "n < 0");
+  if (int rc = check_cache(cache, seq_lens != nullptr && req_idx != nullptr, k_pe != nullptr)) return rc;
+  if (n == 0) return ROLAQ_OK;
+  const int d = cache->latent_dim;
+  if (!c_kv || !slots || !rot_t) return fail(ROLAQ_EINVAL, "NULL pointer");
+  if (!aligned16(c_kv) || ld_ckv < d || ld_ckv % 8)
+    return fail(ROLAQ_EINVAL, "c_kv must be 16-byte aligned with ld_ckv >= D and ld_ckv %% 8 == 0");
+  if (k_pe && (!aligned16(k_pe) || ld_pe < cache->rope_dim || ld_pe % 8))
+    return fail(ROLAQ_EINVAL, "k_pe must be 16-byte aligned with ld_pe >= Dr and ld_pe %% 8 == 0");
+  if (!aligned16(rot_t)) return fail(ROLAQ_EINVAL, "rot_t must be 16-byte aligned");
+  if (n >= (int64_t(1) << 31)) return fail(ROLAQ_EINVAL, "n too large");
+  if (int rc = codec_ok(codec)) return rc;
+  WriterArgs a{};
+  a.n = n;
+  a.d = d;
+  a.k_pe = k_pe;
+  a.ld_pe = ld_pe;
+  a.slots = slots;
+  a.seq_lens = seq_lens;
+  a.seq_is64 = seq_lens_is64;
+  a.req_idx = req_idx;
+  a.req_is64 = req_idx_is64;
+  a.positions = positions;
+  a.pos_is64 = positions_is64;
+  a.codec = codec;
+  a.cache = *cache;
+  a.err = err;
+  return cuda_rc(launch_writer(c_kv, ld_ckv, rot_t, a, false, stream), "fused_write");
+}
+
+int rolaq_rotate_rows(const uint16_t* x, int64_t ldx, int64_t n, int32_t latent_dim, const uint16_t* w,
+                      float* out_f32, uint16_t* out_bf16, int64_t ld_out, cudaStream_t stream) {
+  if (n < 0) return fail(ROLAQ_EINVAL, "n < 0");
+  if (latent_dim != 256 && latent_dim != 512)
+    return fail(ROLAQ_EUNSUPPORTED, "latent_dim %d unsupported (256 or 512)", latent_dim);
+  if (n == 0) return ROLAQ_OK;
+  if (!x || !w || (!out_f32 && !out_bf16)) return fail(ROLAQ_EINVAL, "NULL pointer");
+  if (!aligned16(x) || ldx < latent_dim || ldx % 8) return fail(ROLAQ_EINVAL, "x must be 16-byte aligned, ldx %% 8 == 0");
+  if (!aligned16(w)) return fail(ROLAQ_EINVAL, "w must be 16-byte aligned");
+  if (ld_out < latent_dim || ld_out % 8 || (out_f32 && !aligned16(out_f32)) || (out_bf16 && !aligned16(out_bf16)))
+    return fail(ROLAQ_EINVAL, "outputs must be 16-byte aligned with ld_out %% 8 == 0");
+  WriterArgs a{};
+  a.n = n;
+  a.d = latent_dim;
+  a.out_f32 = out_f32;
+  a.out_bf16 = out_bf16;
+  a.ld_out = ld_out;
+  return cuda_rc(launch_writer(x, ldx, w, a, true, stream), "rotate_rows");
+}
+
+int rolaq_dequant_rows(const uint8_t* codes, const float* params, const void* slots, int slots_are_int64, int64_t n,
+                       int32_t latent_dim, int64_t num_slots, float* out_f32, uint16_t* out_bf16, int64_t ld_out,
+                       int32_t* err, cudaStream_t stream) {
+  if (n < 0) return fail(ROLAQ_EINVAL, "n < 0");
+  if (latent_dim <= 0 || latent_dim % 128) return fail(ROLAQ_EUNSUPPORTED, "latent_dim must be a multiple of 128");
+  if (n == 0) return ROLAQ_OK;
+  if (!codes || !params || (!out_f32 && !out_bf16)) return fail(ROLAQ_EINVAL, "NULL pointer");
+  if (ld_out < latent_dim || ld_out % 4 || (out_f32 && !aligned16(out_f32)) ||
+      (out_bf16 && (reinterpret_cast<uintptr_t>(out_bf16) & 7)))
+    return fail(ROLAQ_EINVAL, "outputs misaligned or ld_out too small");
+  return cuda_rc(launch_dequant(codes, params, slots, slots_are_int64, n, latent_dim, num_slots, out_f32, out_bf16,
+                                ld_out, err, stream),
+                 "dequant_rows");
+}
+
+int rolaq_prepare_gf_splits(const int32_t* splits, int32_t* quant, int32_t* merge, int64_t n, cudaStream_t stream) {
+  if (n < 0) return fail(ROLAQ_EINVAL, "n < 0");
+  if (n == 0) return ROLAQ_OK;
+  if (!splits || !quant || !merge) return fail(ROLAQ_EINVAL, "NULL pointer");
+  return cuda_rc(launch_prepare_splits(splits, quant, merge, n, stream), "prepare_gf_splits");
+}
+
+int rolaq_packed_decode(const uint16_t* q, int64_t q_stride_b, int64_t q_stride_h, int32_t batch, int32_t heads,
+                        const rolaq_layer_cache* cache, const int32_t* page_table, int64_t pt_stride,
+                        int32_t max_pages, const int32_t* seq_lens, const int32_t* token_range, float sm_scale,
+                        int32_t num_splits,
+                        float* part_o, float* part_lse, uint16_t* out, int64_t out_stride_b, int64_t out_stride_h,
+                        float* out_lse, int32_t* err, cudaStream_t stream) {
+  if (batch < 0) return fail(ROLAQ_EINVAL, "batch < 0");
+  if (int rc = check_cache(cache, true)) return rc;
+  const int d = cache->latent_dim;
+  if (!((d == 512 && cache->rope_dim == 64 && (heads == 16 || heads == 8)) ||
+        (d == 256 && cache->rope_dim == 32 && (heads == 40 || heads == 16))))
+    return fail(ROLAQ_EUNSUPPORTED, "decode shape D=%d Dr=%d H=%d not built (512/64/{8,16}, 256/32/{16,40})", d,
+                cache->rope_dim, heads);
+  if (cache->sink + cache->recent > 32) return fail(ROLAQ_EUNSUPPORTED, "sink + recent must be <= 32");
+  if (num_splits < 1 || num_splits > 1024) return fail(ROLAQ_EINVAL, "num_splits must be in [1, 1024]");
+  if (!(sm_scale > 0.f)) return fail(ROLAQ_EINVAL, "sm_scale must be > 0");
+  if (batch == 0) return ROLAQ_OK;
+  if (batch > 65535) return fail(ROLAQ_EINVAL, "batch must be <= 65535");
+  if (!q || !page_table || !seq_lens || !part_o || !part_lse || !out) return fail(ROLAQ_EINVAL, "NULL pointer");
+  if (max_pages <= 0 || pt_stride < max_pages) return fail(ROLAQ_EINVAL, "page table shape");
+  if (q_stride_h < d + cache->rope_dim || q_stride_b < heads * q_stride_h)
+    return fail(ROLAQ_EINVAL, "q strides too small");
+  if ((reinterpret_cast<uintptr_t>(q) & 3) || (q_stride_h & 1) || (q_stride_b & 1))
+    return fail(ROLAQ_EINVAL, "q must be 4-byte aligned with even strides");
+  if (out_stride_h < d || out_stride_b < heads * out_stride_h) return fail(ROLAQ_EINVAL, "out strides too small");
+  DecodeArgs a{};
+  a.q = q;
+  a.q_sb = q_stride_b;
+  a.q_sh = q_stride_h;
+  a.batch = batch;
+  a.cache = *cache;
+  a.page_table = page_table;
+  a.pt_stride = pt_stride;
+  a.max_pages = max_pages;
+  a.seq_lens = seq_lens;
+  a.token_range = token_range;
+  a.sm_scale = sm_scale;
+  a.num_splits = num_splits;
+  a.part_o = part_o;
+  a.part_lse = part_lse;
+  a.err = err;
+  int rc = cuda_rc(launch_decode(a, heads, stream), "packed_decode");
+  if (rc != ROLAQ_OK) return rc;
+  const int parts = num_splits + 1;
+  // out rows are (b, h): row r = b * heads + h, at out + b*out_stride_b + h*out_stride_h
+  if (out_stride_b == heads * out_stride_h) {
+    return cuda_rc(launch_merge(part_o, int64_t(parts) * d, d, part_lse, parts, 1, parts, int64_t(batch) * heads, d,
+                                out, nullptr, out_stride_h, out_lse, stream),
+                   "merge");
+  }
+  for (int b = 0; b < batch; ++b) {
+    rc = cuda_rc(launch_merge(part_o + int64_t(b) * heads * parts * d, int64_t(parts) * d, d,
+                              part_lse + int64_t(b) * heads * parts, parts, 1, parts, heads, d,
+                              out + int64_t(b) * out_stride_b, nullptr, out_stride_h,
+                              out_lse ? out_lse + int64_t(b) * heads : nullptr, stream),
+                 "merge");
+    if (rc != ROLAQ_OK) return rc;
+  }
+  return ROLAQ_OK;
+}
+
+int rolaq_merge_partials(const float* part_o, int64_t row_stride, int64_t part_stride, const float* part_lse,
+                         int64_t lse_row_stride, int64_t lse_part_stride, int32_t n_parts, int64_t rows,
+                         int32_t latent_dim, uint16_t* out_bf16, float* out_f32, int64_t ld_out, float* out_lse,
+                         cudaStream_t stream) {
+  if (rows < 0 || n_parts < 1) return fail(ROLAQ_EINVAL, "rows < 0 or n_parts < 1");
+  if (latent_dim <= 0) return fail(ROLAQ_EINVAL, "latent_dim <= 0");
+  if (rows == 0) return ROLAQ_OK;
+  if (!part_o || !part_lse) return fail(ROLAQ_EINVAL, "NULL pointer");
+  if ((out_bf16 || out_f32) && ld_out < latent_dim) return fail(ROLAQ_EINVAL, "ld_out too small");
+  if (rows > 0x7FFFFFFF) return fail(ROLAQ_EINVAL, "too many rows");
+  return cuda_rc(launch_merge(part_o, row_stride, part_stride, part_lse, lse_row_stride, lse_part_stride, n_parts,
+                              rows, latent_dim, out_bf16, out_f32, ld_out, out_lse, stream),
+                 "merge");
+}
+
+}  // extern "C"

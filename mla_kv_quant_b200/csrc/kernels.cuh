@@ -1,0 +1,80 @@
+// Argument blocks and launchers shared between the kernel translation units and
+// the C ABI (abi.cu).  Internal to the library.
+#pragma once
+
+#include "common.cuh"
+
+namespace rolaq {
+
+// Fused writer / rotation GEMM (writer.cu).
+struct WriterArgs {
+  int64_t n;
+  int32_t d;
+  // codec mode
+  const uint16_t* k_pe;
+  int64_t ld_pe;
+  const int64_t* slots;
+  const void* seq_lens;
+  int seq_is64;
+  const void* req_idx;
+  int req_is64;
+  const void* positions;
+  int pos_is64;
+  rolaq_codec codec;
+  rolaq_layer_cache cache;
+  int32_t* err;
+  // plain (rotation-only) mode
+  float* out_f32;
+  uint16_t* out_bf16;
+  int64_t ld_out;
+};
+
+// Packed decode (decode.cu).
+struct DecodeArgs {
+  const uint16_t* q;
+  int64_t q_sb, q_sh;
+  int32_t batch;
+  rolaq_layer_cache cache;
+  const int32_t* page_table;
+  int64_t pt_stride;
+  int32_t max_pages;
+  const int32_t* seq_lens;
+  const int32_t* token_range;  // [B, 2] or nullptr
+  float sm_scale;
+  int32_t num_splits;
+  float* part_o;
+  float* part_lse;
+  int32_t* err;
+};
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// abi.cu
+EncodeTiledFn encode_fn();
+int sm_count();
+
+// writer.cu
+int launch_writer(const uint16_t* x, int64_t ldx, const uint16_t* w, const WriterArgs& args, bool plain,
+                  cudaStream_t stream);
+
+// codec.cu
+int launch_scatter_pack(const float* x, int64_t ldx, const void* slots, int slots64, int64_t n, int d,
+                        rolaq_codec codec, uint8_t* codes, float* params, int64_t num_slots, int32_t* err,
+                        cudaStream_t s);
+int launch_aux(const float* c, int64_t ldc, const uint16_t* k_pe, int64_t ld_pe, const int64_t* slots,
+               const void* seq, int seq64, const void* req, int req64, const void* pos, int pos64, int64_t n,
+               const rolaq_layer_cache& cache, int32_t* err, cudaStream_t s);
+int launch_dequant(const uint8_t* codes, const float* params, const void* slots, int slots64, int64_t n, int d,
+                   int64_t num_slots, float* out_f32, uint16_t* out_bf16, int64_t ld_out, int32_t* err,
+                   cudaStream_t s);
+int launch_prepare_splits(const int32_t* splits, int32_t* quant, int32_t* merge, int64_t n, cudaStream_t s);
+
+// decode.cu
+int launch_decode(const DecodeArgs& a, int heads, cudaStream_t s);
+int launch_merge(const float* part_o, int64_t row_stride, int64_t part_stride, const float* part_lse,
+                 int64_t lse_row_stride, int64_t lse_part_stride, int n_parts, int64_t rows, int d,
+                 uint16_t* out_bf16, float* out_f32, int64_t ld_out, float* out_lse, cudaStream_t s);
+
+}  // namespace rolaq

@@ -1,0 +1,387 @@
+// Fused packed-INT2 cache writer for sm_100a.
+//
+// c = c_kv @ R runs on tcgen05 tensor cores: BF16 operands are staged in shared
+// memory by TMA (128-byte swizzle), one elected thread issues kind::f16 MMAs into a
+// double-buffered FP32 accumulator in tensor memory, and eight epilogue warps read
+// the accumulator back (tcgen05.ld) to run the Lloyd INT2 codec, pack 4 codes per
+// byte, scatter codes/params by slot, and write k_pe and the s4r16 window rows.
+//
+// Reference behaviour: deployment/sglang/QuantKernel/mla_fused_writer.py:54-224
+// (FP32 GEMM + Triton _pack_and_aux) and mla_quant/oscar.py:120-144 (codec).
+//
+// CTA tile: 128 rows x 256 latent columns (two 128-wide quantisation groups).  A row
+// of D = 512 is covered by two tiles; adjacent CTAs take the two halves of the same
+// rows so the second read of those rows hits L2.
+#include "kernels.cuh"
+
+namespace rolaq {
+
+constexpr int kTileM = 128;
+constexpr int kTileN = 256;
+constexpr int kTileK = 64;  // one 128-byte swizzle row of BF16
+constexpr int kStages = 4;
+constexpr int kABytes = kTileM * kTileK * 2;  // 16 KB
+constexpr int kBBytes = kTileN * kTileK * 2;  // 32 KB
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kWriterThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
+constexpr int kEpiThreads = 256;
+constexpr uint32_t kTmemCols = 512;  // two 256-column accumulators
+constexpr size_t kWriterSmem = size_t(kStages) * kStageBytes + 1024 + 256;
+
+// Per-row bookkeeping shared by the codec epilogue warps of one row.
+struct RowMeta {
+  int64_t slot;
+  int64_t ring;  // -1: not a window row
+  bool ok;       // slot in range
+};
+
+__device__ __forceinline__ RowMeta row_meta(const WriterArgs& a, int64_t row) {
+  RowMeta m{0, -1, false};
+  const int64_t slot = a.slots[row];
+  m.slot = slot;
+  m.ok = slot >= 0 && slot < a.cache.num_slots;
+  const int P = a.cache.sink, W = a.cache.recent;
+  if (m.ok && slot > 0 && a.seq_lens != nullptr && a.req_idx != nullptr && a.cache.rows != nullptr &&
+      (P + W) > 0) {
+    const int64_t seq = load_index(a.seq_lens, a.seq_is64, row);
+    const int64_t req = load_index(a.req_idx, a.req_is64, row);
+    const int64_t pos = a.positions ? load_index(a.positions, a.pos_is64, row) : seq - 1;
+    const bool keep = (pos < P || pos >= seq - W) && req >= 0 && req < a.cache.max_reqs && pos >= 0;
+    if (keep) {
+      const int64_t w = W > 0 ? W : 1;
+      const int64_t inner = pos < P ? pos : P + ((pos - P) > 0 ? (pos - P) : 0) % w;
+      const int64_t ring = 1 + req * (P + W) + inner;
+      m.ring = ring < a.cache.num_ring_rows ? ring : -1;
+    }
+  }
+  return m;
+}
+
+template <bool kPlain>
+__global__ void __launch_bounds__(kWriterThreads, 1)
+    writer_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                  const WriterArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int d = args.d;
+  const int halves = d / kTileN;
+  const int64_t row_tiles = (args.n + kTileM - 1) / kTileM;
+  const int64_t tiles = row_tiles * halves;
+  const int kchunks = d / kTileK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kEpiThreads);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tensormap(&tmap_x);
+    prefetch_tensormap(&tmap_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---- TMA producer -------------------------------------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+        const int32_t row0 = static_cast<int32_t>((t / halves) * kTileM);
+        const int32_t col0 = static_cast<int32_t>((t % halves) * kTileN);
+        for (int kc = 0; kc < kchunks; ++kc) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, args.err)) {
+            *abort_flag = 1;
+            break;
+          }
+          uint8_t* a_s = smem + stage * kStageBytes;
+          uint8_t* b_s = a_s + kABytes;
+          mbar_expect_tx(&full[stage], kStageBytes);
+          tma_load_2d(a_s, &tmap_x, &full[stage], kc * kTileK, row0);
+          tma_load_2d(b_s, &tmap_w, &full[stage], kc * kTileK, col0);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (*(volatile int*)abort_flag) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer -----------------------------------------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      const uint32_t idesc = idesc_bf16(kTileM, kTileN);
+      int64_t lt = 0;
+      for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++lt) {
+        const int buf = static_cast<int>(lt & 1);
+        const uint32_t use = static_cast<uint32_t>(lt >> 1);
+        if (!mbar_wait(&tempty[buf], (use & 1u) ^ 1u, args.err)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kTileN);
+        bool ok = true;
+        for (int kc = 0; kc < kchunks; ++kc) {
+          if (!mbar_wait(&full[stage], phase, args.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * kStageBytes);
+          const uint32_t b_addr = a_addr + kABytes;
+#pragma unroll
+          for (int k = 0; k < kTileK / 16; ++k) {
+            umma_bf16_ss(d_tmem, sw128_kmajor_desc(a_addr + k * 32), sw128_kmajor_desc(b_addr + k * 32), idesc,
+                         (kc | k) != 0);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) {
+          *abort_flag = 1;
+          break;
+        }
+        umma_commit(&tfull[buf]);
+      }
+    }
+  } else {
+    // ---- epilogue: 8 warps; warp w reads TMEM lanes 32*(w%4).. and group (w-2)/4 -----
+    const int quad = warp & 3;
+    const int sub = (warp - 2) >> 2;
+    int64_t lt = 0;
+    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++lt) {
+      const int buf = static_cast<int>(lt & 1);
+      const uint32_t use = static_cast<uint32_t>(lt >> 1);
+      if (!mbar_wait(&tfull[buf], use & 1u, args.err)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int64_t row = (t / halves) * kTileM + quad * 32 + lane;
+      const int half = static_cast<int>(t % halves);
+      const int group = half * 2 + sub;  // global 128-column group index
+      const bool valid = row < args.n;
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(buf * kTileN + sub * 128);
+      uint32_t r[32];
+
+      if constexpr (kPlain) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32(taddr + c * 32, r);
+          tmem_wait_ld();
+          if (valid) {
+            const int64_t col = group * 128 + c * 32;
+            if (args.out_f32) {
+              float4* dst = reinterpret_cast<float4*>(args.out_f32 + row * args.ld_out + col);
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                     __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+            }
+            if (args.out_bf16) {
+              uint4* dst = reinterpret_cast<uint4*>(args.out_bf16 + row * args.ld_out + col);
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                dst[j] = make_uint4(pack_bf16x2(__uint_as_float(r[8 * j]), __uint_as_float(r[8 * j + 1])),
+                                    pack_bf16x2(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3])),
+                                    pack_bf16x2(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5])),
+                                    pack_bf16x2(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7])));
+            }
+          }
+        }
+      } else {
+        // pass 1: mean
+        GroupSum acc;
+        acc.zero();
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32(taddr + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc.add(j & 7, __uint_as_float(r[j]));
+        }
+        const float mean = __fmul_rn(acc.total(), 1.0f / 128.0f);
+        // pass 2: population variance of the centred values
+        acc.zero();
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32(taddr + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float df = __fsub_rn(__uint_as_float(r[j]), mean);
+            acc.add(j & 7, __fmul_rn(df, df));
+          }
+        }
+        const float var = __fmul_rn(acc.total(), 1.0f / 128.0f);
+        const float stdv = __fsqrt_rn(__fadd_rn(var, 1e-8f));
+        const float rstd = __frcp_rn(stdv);
+        const float thr = args.codec.threshold;
+        const bool exact_all = !(stdv < 1e30f);
+        // pass 3: codes.  n ~= diff * (1/std) decides every element whose |n| is not
+        // within 2^-20 relative of t; the rest use the IEEE quotient diff / std, which
+        // is what the reference compares.
+        uint32_t words[8];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32(taddr + c * 32, r);
+          tmem_wait_ld();
+          uint32_t w0 = 0, w1 = 0;
+          bool amb = false;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float df = __fsub_rn(__uint_as_float(r[j]), mean);
+            const float a = fabsf(__fmul_rn(df, rstd));
+            const uint32_t hi = (__float_as_uint(df) >> 31) ^ 1u;  // df >= 0 (also -0.0)
+            const uint32_t lo = hi ^ static_cast<uint32_t>(a < thr);
+            amb |= fabsf(a - thr) <= a * 9.5367431640625e-07f || a < 1e-30f;
+            const uint32_t code = (hi << 1) | lo;
+            if (j < 16)
+              w0 |= code << (2 * j);
+            else
+              w1 |= code << (2 * (j - 16));
+          }
+          if (amb || exact_all) {
+            w0 = 0;
+            w1 = 0;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float df = __fsub_rn(__uint_as_float(r[j]), mean);
+              const uint32_t code = lloyd_code(df, stdv, thr);
+              if (j < 16)
+                w0 |= code << (2 * j);
+              else
+                w1 |= code << (2 * (j - 16));
+            }
+          }
+          words[2 * c] = w0;
+          words[2 * c + 1] = w1;
+        }
+        const float scale = __fmul_rn(args.codec.scale_factor, stdv);
+        const float zero = __fsub_rn(args.codec.zero_const, __fdiv_rn(mean, scale));
+        RowMeta m{0, -1, false};
+        if (valid) m = row_meta(args, row);
+        if (valid && !m.ok && sub == 0 && half == 0) report(args.err, ROLAQ_DEV_BAD_SLOT);
+        if (valid && m.ok) {
+          uint4* cdst = reinterpret_cast<uint4*>(args.cache.codes + m.slot * (d / 4) + group * 32);
+          cdst[0] = make_uint4(words[0], words[1], words[2], words[3]);
+          cdst[1] = make_uint4(words[4], words[5], words[6], words[7]);
+          float2* pdst = reinterpret_cast<float2*>(args.cache.params + (m.slot * (d / 128) + group) * 2);
+          *pdst = make_float2(scale, zero);
+          if (sub == 0 && half == 0 && m.slot > 0) {
+            // k_pe and the slot <-> ring maps, once per row
+            if (args.k_pe != nullptr) {
+              const int dr = args.cache.rope_dim;
+              const uint4* src = reinterpret_cast<const uint4*>(args.k_pe + row * args.ld_pe);
+              uint4* dst = reinterpret_cast<uint4*>(args.cache.rope + m.slot * dr);
+              for (int j = 0; j < dr / 8; ++j) dst[j] = src[j];
+            }
+            if (args.cache.rows != nullptr && args.seq_lens != nullptr && args.req_idx != nullptr) {
+              args.cache.rows[m.slot] = static_cast<int32_t>(m.ring);
+              if (m.ring >= 0) args.cache.owners[m.ring] = static_cast<int32_t>(m.slot);
+            }
+          }
+        }
+        // Window rows: BF16 rotated latent into the ring.  The TMEM loads are
+        // warp-collective, so the whole warp reloads when any lane needs it.
+        if (__any_sync(0xFFFFFFFFu, m.ring >= 0)) {
+          uint4* hdst = m.ring >= 0 ? reinterpret_cast<uint4*>(args.cache.hp + m.ring * d + group * 128) : nullptr;
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            tmem_ld32(taddr + c * 32, r);
+            tmem_wait_ld();
+            if (hdst != nullptr) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                hdst[c * 4 + j] =
+                    make_uint4(pack_bf16x2(__uint_as_float(r[8 * j]), __uint_as_float(r[8 * j + 1])),
+                               pack_bf16x2(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3])),
+                               pack_bf16x2(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5])),
+                               pack_bf16x2(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7])));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---- host side -----------------------------------------------------------------------
+
+// 2-D BF16 (or byte) tensor map over a row-major matrix, 128-byte swizzle.
+int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t inner,
+                uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return ROLAQ_ECUDA;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  (void)elem_bytes;
+  CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? ROLAQ_OK : ROLAQ_ECUDA;
+}
+
+int launch_writer(const uint16_t* x, int64_t ldx, const uint16_t* w, const WriterArgs& args, bool plain,
+                  cudaStream_t stream) {
+  CUtensorMap mx, mw;
+  const int d = args.d;
+  if (args.n <= 0) return ROLAQ_OK;
+  int rc = make_map_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, static_cast<uint64_t>(d),
+                       static_cast<uint64_t>(args.n), static_cast<uint64_t>(ldx) * 2, kTileK, kTileM);
+  if (rc != ROLAQ_OK) return rc;
+  rc = make_map_2d(&mw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, static_cast<uint64_t>(d), static_cast<uint64_t>(d),
+                   static_cast<uint64_t>(d) * 2, kTileK, kTileN);
+  if (rc != ROLAQ_OK) return rc;
+  const int64_t tiles = ((args.n + kTileM - 1) / kTileM) * (d / kTileN);
+  const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
+  if (plain) {
+    cudaFuncSetAttribute(writer_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kWriterSmem);
+    writer_kernel<true><<<grid, kWriterThreads, kWriterSmem, stream>>>(mx, mw, args);
+  } else {
+    cudaFuncSetAttribute(writer_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kWriterSmem);
+    writer_kernel<false><<<grid, kWriterThreads, kWriterSmem, stream>>>(mx, mw, args);
+  }
+  return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;
+}
+
+}  // namespace rolaq
