@@ -1,0 +1,476 @@
+"""Benchmark of the packed-INT2 MLA cache path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline (BASELINE.json metric "INT2 MLA decode-attn tok/s @B64,16K ctx; writer GB/s
+vs HBM peak"): one *step* is one decode step of DeepSeek-V2-Lite's 27 MLA layers for
+64 requests at 16384 tokens of context: per layer, the fused writer stores the 64 new
+latents (tcgen05 rotation + INT2 codec + k_pe + s4r16 ring), then packed decode
+attention reads the INT2 cache.  ``value`` = whole-job tokens/s (N x 64 tokens per step)
+with everything resident in HBM (the step replayed from a CUDA graph); ``e2e`` = the
+same step through the public plugin API (``try_fast_decode_store``,
+``packed_mla_decode_gf_fwd``) with the per-step queries / new latents copied from
+pinned host memory and the outputs copied back, inside the timed region.  The
+``writer`` object reports the config-1 prefill writer (27 layers x 8 x 16384 rows).
+
+Data are seeded synthetic tensors with the benchmark distributions (no dataset or
+checkpoint).  Multi-GPU (torchrun): every rank serves its own 64 requests (request
+sharding, weak scaling, no data-path collective); time is the max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "INT2 MLA decode-attn tok/s @B64,16K ctx; writer GB/s vs HBM peak"
+LAYERS, HEADS, D, DR = 27, 16, 512, 64
+SINK, RECENT = 4, 16
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        j = json.loads(p.read_text())
+        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), float(j.get("bf16_tflops_sustained", j["bf16_tflops"])), "measured"
+    return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, 1400.0, "fallback"
+
+
+def decode_bytes(batch, ctx, heads=HEADS, d=D, dr=DR, window=SINK + RECENT):
+    """Algorithmic HBM bytes of one decode launch (one layer)."""
+    per_int2 = d // 4 + (d // 128) * 8 + dr * 2  # 288 B: codes + (scale, zero) + k_pe
+    per_win = d * 2 + dr * 2 + 8  # BF16 ring row + k_pe + slot/ring maps
+    win = min(window, ctx)
+    return batch * ((ctx - win) * per_int2 + win * per_win) + batch * heads * ((d + dr) * 2 + d * 2)
+
+
+def writer_bytes(rows, d=D, dr=DR):
+    """Algorithmic HBM bytes of one writer launch: c_kv + k_pe + slot in, codes + params + k_pe out."""
+    return rows * ((2 * d + 2 * dr + 8) + (d // 4 + (d // 128) * 8 + 2 * dr))
+
+
+def read_traffic():
+    """Per-launch DRAM bytes of the decode kernel from the committed ncu summary (or None)."""
+    f = ROOT / "profiles" / "decode_b64_ctx16k.md"
+    if not f.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read_text())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples while the timed region runs."""
+
+    def __init__(self, dev: torch.device):
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+        self.index = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        self.proc = None
+        self.out = None
+
+    def __enter__(self):
+        self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.out,
+                                         stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.2)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in Path(self.out.name).read_text().splitlines():
+                f = [x.strip() for x in line.split(",")]
+                if len(f) >= 9:
+                    rows.append(f)
+        finally:
+            os.unlink(self.out.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------------
+
+
+def build_state(dev, batch, ctx, seed):
+    from mla_kv_quant_b200 import ops, synth
+    from mla_kv_quant_b200.pool import PackedLatentPool
+
+    rot = {i: synth.rotation(D, 1000 + i) for i in range(LAYERS)}
+    params = synth.layer_params(LAYERS, seed=2)
+    pages = (ctx + 63) // 64
+    pt, num_slots = synth.page_table(batch, ctx, seed=4 + seed, device=dev)
+    pool = PackedLatentPool(num_slots, LAYERS, D, DR, max_reqs=batch, sink=SINK, recent=RECENT, device=dev,
+                            rotations=rot, quantizer_params=params)
+    return pool, pt, pages
+
+
+def fill_cache(pool, pt, batch, ctx, dev, seed, writer_timing=None):
+    """Prefill every layer: 8 requests x ctx rows per writer launch (config-1 shape)."""
+    from mla_kv_quant_b200 import ops, synth
+
+    scale = synth.channel_scale(D, 77, dev)
+    chunk = 8
+    pos = torch.arange(ctx, device=dev)
+    for li in range(LAYERS):
+        rt = pool.write_rotation_t(li)
+        codec = pool.codec(li)
+        view = pool.layer_view(li)
+        for b0 in range(0, batch, chunk):
+            bs = list(range(b0, min(batch, b0 + chunk)))
+            n = len(bs) * ctx
+            x = synth.latents(n, D, seed + 131 * li + b0, dev, scale=scale)
+            pe = synth.normal_bf16((n, DR), seed + 7 * li + b0 + 1, dev)
+            slots = torch.cat([pt[b, pos // 64].long() * 64 + pos % 64 for b in bs])
+            seq = torch.full((n,), ctx, dtype=torch.int32, device=dev)
+            req = torch.cat([torch.full((ctx,), b, dtype=torch.int64, device=dev) for b in bs])
+            p = pos.repeat(len(bs)).to(torch.int32)
+            ops.fused_write(x, pe, slots, rt, codec, view, seq_lens=seq, req_idx=req, positions=p)
+    torch.cuda.synchronize()
+
+
+def time_writer(pool, dev, ctx, warmup, iters):
+    """Config 1: 27 layers x (8 x ctx) prefill rows through the fused writer."""
+    from mla_kv_quant_b200 import ops, synth
+
+    n = 8 * ctx
+    x = synth.latents(n, D, 5, dev)
+    pe = synth.normal_bf16((n, DR), 6, dev)
+    slots = torch.arange(64, 64 + n, device=dev, dtype=torch.int64)
+    pos = torch.arange(ctx, device=dev, dtype=torch.int32).repeat(8)
+    seq = torch.full((n,), ctx, dtype=torch.int32, device=dev)
+    req = torch.arange(8, device=dev).repeat_interleave(ctx)
+    views = [pool.layer_view(li) for li in range(LAYERS)]
+    rts = [pool.write_rotation_t(li) for li in range(LAYERS)]
+    codecs = [pool.codec(li) for li in range(LAYERS)]
+
+    def run():
+        for li in range(LAYERS):
+            ops.fused_write(x, pe, slots, rts[li], codecs[li], views[li], seq_lens=seq, req_idx=req, positions=pos)
+
+    for _ in range(warmup):
+        run()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        run()
+    e.record()
+    torch.cuda.synchronize()
+    per_launch_s = s.elapsed_time(e) / 1e3 / (iters * LAYERS)
+    return n, per_launch_s
+
+
+def run_ours(args, rank, world, dev):
+    from mla_kv_quant_b200 import ops, synth
+    from mla_kv_quant_b200.mla_fused_writer import try_fast_decode_store
+    from mla_kv_quant_b200.mla_packed_decode import packed_mla_decode_gf_fwd
+
+    batch, ctx = args.batch, args.ctx
+    hbm, tf_burst, tf_sus, peak_kind = peaks()
+    pool, pt, pages = build_state(dev, batch, ctx, seed=rank)
+    fill_cache(pool, pt, batch, ctx, dev, seed=100 * rank)
+    splits = args.splits or ops.default_num_splits(batch, ctx)
+    sm_scale = 1.0 / math.sqrt(192.0)
+
+    # per-step inputs: queries per layer and one new latent row per request per layer
+    q = synth.normal_bf16((LAYERS, batch, HEADS, D + DR), 11 + rank, dev)
+    new_ckv = synth.latents(LAYERS * batch, D, 12 + rank, dev).view(LAYERS, batch, D)
+    new_pe = synth.normal_bf16((LAYERS, batch, DR), 13 + rank, dev)
+    out = torch.empty(LAYERS, batch, HEADS, D, dtype=torch.bfloat16, device=dev)
+    seq = torch.full((batch,), ctx, dtype=torch.int32, device=dev)
+    req = torch.arange(batch, device=dev, dtype=torch.int64)
+    last = ctx - 1
+    loc = (pt[:, last // 64].long() * 64 + last % 64).contiguous()
+    part_o = torch.empty(batch, HEADS, splits + 1, D, device=dev)
+    part_lse = torch.empty(batch, HEADS, splits + 1, device=dev)
+    views = [pool.layer_view(li) for li in range(LAYERS)]
+    rts = [pool.write_rotation_t(li) for li in range(LAYERS)]
+    codecs = [pool.codec(li) for li in range(LAYERS)]
+    dec_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(LAYERS)]
+
+    def step(timed_events=False):
+        for li in range(LAYERS):
+            ops.fused_write(new_ckv[li], new_pe[li], loc, rts[li], codecs[li], views[li], seq_lens=seq, req_idx=req)
+            if timed_events:
+                dec_ev[li][0].record()
+            ops.packed_decode(q[li], views[li], pt, seq, sm_scale, splits, part_o, part_lse, out[li])
+            if timed_events:
+                dec_ev[li][1].record()
+
+    # decode-kernel roofline: events around each decode launch (eager, same stream)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dec_times = []
+    for _ in range(max(3, args.steps // 10)):
+        step(timed_events=True)
+        torch.cuda.synchronize()
+        dec_times += [a.elapsed_time(b) / 1e3 for a, b in dec_ev]
+    dec_s = statistics.mean(dec_times)
+
+    # value: the step replayed from a CUDA graph
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clk:
+        s.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    step_s = s.elapsed_time(e) / 1e3 / args.steps
+    step_s = max_over_ranks(step_s, world, dev)
+    clocks = clk.summary()
+    del graph
+
+    # e2e: public API, host buffers, copies inside the timed region
+    pool.set_window_meta(True, seq, req)
+    pool._rolaq_fused_decode_write = True
+    h_q = q.cpu().pin_memory()
+    h_ckv = new_ckv.cpu().pin_memory()
+    h_pe = new_pe.cpu().pin_memory()
+    h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    d_q, d_ckv, d_pe = torch.empty_like(q[0]), torch.empty_like(new_ckv[0]), torch.empty_like(new_pe[0])
+
+    def e2e_step():
+        for li in range(LAYERS):
+            d_ckv.copy_(h_ckv[li], non_blocking=True)
+            d_pe.copy_(h_pe[li], non_blocking=True)
+            d_q.copy_(h_q[li], non_blocking=True)
+            if not try_fast_decode_store(pool, li, loc, d_ckv, d_pe):
+                raise RuntimeError("fused decode writer declined a decode step")
+            packed_mla_decode_gf_fwd(d_q, pool, li, pt, seq, sm_scale, splits, attn_logits=part_o,
+                                     attn_lse=part_lse, out=out[li])
+            h_out[li].copy_(out[li], non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e.record()
+    torch.cuda.synchronize()
+    e2e_s = max_over_ranks(s.elapsed_time(e) / 1e3 / args.steps, world, dev)
+    h2d = LAYERS * (q[0].numel() * 2 + new_ckv[0].numel() * 2 + new_pe[0].numel() * 2)
+    d2h = LAYERS * out[0].numel() * 2
+
+    # writer leg (config 1), rank-local
+    wrows, w_s = time_writer(pool, dev, ctx, warmup=2, iters=max(3, min(10, args.steps // 20)))
+    w_bytes = writer_bytes(wrows)
+    w_flops = 2.0 * wrows * D * D
+
+    dbytes = decode_bytes(batch, ctx)
+    achieved = dbytes / dec_s / 1e9
+    res = {
+        "metric": METRIC,
+        "value": world * batch / step_s,
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": step_s * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded; latents N(0,1) x lognormal(0,0.5) channel scale, 8 outlier channels x10)",
+        "config": {
+            "workload": f"decode step: {LAYERS} MLA layers (DeepSeek-V2-Lite shape) x batch {batch} x ctx {ctx}, "
+                        "fused decode write + packed INT2 decode attention per layer",
+            "batch_per_gpu": batch, "global_batch": batch * world, "ctx": ctx, "layers": LAYERS, "heads": HEADS,
+            "kv_lora_rank": D, "rope_dim": DR, "window": "s4r16", "page": 64, "num_splits": splits,
+            "l2": "no flush: per-step working set %.1f GB >> 126 MB L2" % (LAYERS * dbytes / 1e9),
+            "parallelism": f"dp{world} (request-sharded, no collective)",
+        },
+        "e2e": {"value": world * batch / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_s * 1e3,
+                "path": "try_fast_decode_store + packed_mla_decode_gf_fwd, eager, pinned host buffers"},
+        "roofline": {"kernel": "rolaq decode (decode_kernel + merge_kernel), one layer", "bound": "hbm",
+                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_source": f"{peak_kind} hbm_gbs", "traffic": read_traffic(),
+                     "algorithmic_bytes_per_launch": dbytes, "launch_us": dec_s * 1e6},
+        "writer": {"rows_per_launch": wrows, "launch_us": w_s * 1e6, "gbs": w_bytes / w_s / 1e9,
+                   "hbm_frac": (w_bytes / w_s / 1e9) / hbm, "tflops": w_flops / w_s / 1e12,
+                   "tensor_frac": (w_flops / w_s / 1e12) / tf_burst,
+                   "roofline_frac": max(w_bytes / (hbm * 1e9), w_flops / (tf_burst * 1e12)) / w_s,
+                   "bound": "tensor" if w_flops / (tf_burst * 1e12) > w_bytes / (hbm * 1e9) else "hbm",
+                   "note": "roofline_frac = max(bytes/HBM peak, flops/bf16 peak) / time, of " + peak_kind},
+        "clocks": clocks,
+        "gpu_launches": args.steps * LAYERS * 3,
+    }
+    return res
+
+
+def max_over_ranks(x, world, dev):
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------------------------
+# CPU baseline (the oracle port of the reference algorithm on the host cores)
+# ---------------------------------------------------------------------------------------------
+
+
+def cpu_decode_sample(batch_sample=2, ctx=16384, seed=0):
+    """Time the oracle decode (FP32 numpy, all host threads) for `batch_sample`
+    requests of one layer; return seconds per (request, layer)."""
+    from oracle import codec as ocodec
+    from oracle import decode as odecode
+    from oracle import writer as owriter
+
+    rng = np.random.default_rng(seed)
+    pages = (ctx + 63) // 64
+    pool = owriter.Pool((batch_sample * pages + 1) * 64, D, DR, batch_sample, SINK, RECENT)
+    n = pool.num_slots
+    pool.codes[:] = rng.integers(0, 256, size=pool.codes.shape, dtype=np.uint8)
+    pool.params[..., 0] = rng.uniform(0.5, 1.5, size=pool.params.shape[:2]).astype(np.float32)
+    pool.params[..., 1] = rng.uniform(0.0, 3.0, size=pool.params.shape[:2]).astype(np.float32)
+    pool.rope[:] = owriter.bf16_bits(rng.standard_normal(pool.rope.shape).astype(np.float32))
+    pt = (np.arange(batch_sample * pages) + 1).reshape(batch_sample, pages).astype(np.int32)
+    q = owriter.bf16_bits(rng.standard_normal((batch_sample, HEADS, D + DR)).astype(np.float32))
+    odecode.decode(pool, q, pt[:, :1], [64] * batch_sample, 0.07, dtype=np.float32)  # warm-up
+    t0 = time.perf_counter()
+    odecode.decode(pool, q, pt, [ctx] * batch_sample, 1 / math.sqrt(192), dtype=np.float32)
+    dt = time.perf_counter() - t0
+    del ocodec
+    return dt / batch_sample
+
+
+def cpu_baseline(batch, ctx):
+    per = cpu_decode_sample(2, ctx)
+    step = per * batch * LAYERS
+    return {"value": batch / step, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"oracle.decode (numpy FP32, BLAS on all {os.cpu_count()} host threads): 2 requests x 1 layer "
+                      f"x ctx {ctx}, scaled to {batch} requests x {LAYERS} layers per step"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    batch, ctx = args.batch, args.ctx
+    for _ in range(args.warmup):
+        cpu_decode_sample(1, ctx)
+    times = []
+    for _ in range(args.steps_ref):
+        times.append(cpu_decode_sample(1, ctx) * batch * LAYERS)
+    step = statistics.median(times)
+    val = batch / step
+    return {
+        "metric": METRIC, "impl": "reference", "value": val, "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps_ref, "warmup": args.warmup, "ms_per_step": step * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"decode step: {LAYERS} layers x batch {batch} x ctx {ctx} (sampled: 1 request x "
+                               "1 layer per step, scaled)", "batch_per_gpu": batch, "ctx": ctx,
+                   "parallelism": "host CPU, one process"},
+        "cpu_baseline": {"value": val, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": "oracle.decode (numpy FP32, all host threads), 1 request x 1 layer per step"},
+        "e2e": {"value": val, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--ctx", type=int, default=16384)
+    ap.add_argument("--splits", type=int, default=0, help="INT2 KV splits per request (0: auto)")
+    ap.add_argument("--steps-ref", type=int, default=3, help="timed samples of the reference arm")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if world > 1:
+            # only rank 0 runs the CPU reference; the other ranks exit without work
+            if rank != 0:
+                return 0
+        res = run_reference(args, rank, world)
+        print(json.dumps(res))
+        return 0
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    res = run_ours(args, rank, world, dev)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline(args.batch, args.ctx)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

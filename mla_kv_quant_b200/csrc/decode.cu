@@ -23,7 +23,14 @@
 
 namespace rolaq {
 
-constexpr uint32_t kMagic = 0x43004300u;  // BF16x2 {128, 128}
+constexpr uint32_t kMagic = 0x43004300u;    // BF16x2 {128, 128}: QK codes, 128 + c
+constexpr uint32_t kMagic16 = 0x64006400u;  // FP16x2 {1024, 1024}: PV codes, 1024 + c
+
+__device__ __forceinline__ uint32_t hsub_magic16(uint32_t v) {
+  __half2 h = *reinterpret_cast<__half2*>(&v);
+  h = __hsub2(h, __half2half2(__ushort_as_half(0x6400)));
+  return *reinterpret_cast<uint32_t*>(&h);
+}
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int kPage = 64;
@@ -372,7 +379,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
         const float2 sz = reinterpret_cast<const float2*>(ps)[tok * NG + gr];
         sc[rr][gr] = sz.x;
         ze[rr][gr] = sz.y;
-        zp[rr][gr] = 128.f + sz.y;
+        zp[rr][gr] = sz.y;
       }
 #pragma unroll
       for (int t = 0; t < HN; ++t)
@@ -431,10 +438,13 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
 #pragma unroll
         for (int rr = 0; rr < 2; ++rr) {
           const int tok = rr ? tb : ta;
-          const uint32_t pp = pack_bf16x2(s2[rr][t][0] * sc[rr][gr], s2[rr][t][1] * sc[rr][gr]);
-          *reinterpret_cast<uint32_t*>(pw + (gr * kPage + tok) * C::PSTRIDE + 8 * t + 2 * qi) = pp;
-          y_part[gr][t][0] = fmaf(bf16_lo(pp), zp[rr][gr], y_part[gr][t][0]);
-          y_part[gr][t][1] = fmaf(bf16_hi(pp), zp[rr][gr], y_part[gr][t][1]);
+          // P' in FP16 (11-bit significand); the zero-point correction uses the same
+          // rounded values the tensor cores multiply
+          const __half2 ph = __floats2half2_rn(s2[rr][t][0] * sc[rr][gr], s2[rr][t][1] * sc[rr][gr]);
+          *reinterpret_cast<__half2*>(pw + (gr * kPage + tok) * C::PSTRIDE + 8 * t + 2 * qi) = ph;
+          const float2 pf = __half22float2(ph);
+          y_part[gr][t][0] = fmaf(pf.x, zp[rr][gr], y_part[gr][t][0]);
+          y_part[gr][t][1] = fmaf(pf.y, zp[rr][gr], y_part[gr][t][1]);
         }
       }
     __syncthreads();
@@ -486,12 +496,14 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
       for (int mt = 0; mt < C::MT; ++mt) {
         const uint32_t r1 = prmt(wv[0][mt], wv[1][mt], prmt_sel);
         const uint32_t r2 = prmt(wv[2][mt], wv[3][mt], prmt_sel);
-        const uint32_t a0 = lop_and_or(r1 >> psh, 0x00030003u, kMagic);
-        const uint32_t a1 = lop_and_or(r1 >> (psh + 8), 0x00030003u, kMagic);
-        const uint32_t a2 = lop_and_or(r2 >> psh, 0x00030003u, kMagic);
-        const uint32_t a3 = lop_and_or(r2 >> (psh + 8), 0x00030003u, kMagic);
+        // exact FP16 codes: (1024 + c) - 1024.  The offset must not reach the
+        // accumulator, whose additions truncate: 1024 * sum(P') would swamp sum(P' c).
+        const uint32_t a0 = hsub_magic16(lop_and_or(r1 >> psh, 0x00030003u, kMagic16));
+        const uint32_t a1 = hsub_magic16(lop_and_or(r1 >> (psh + 8), 0x00030003u, kMagic16));
+        const uint32_t a2 = hsub_magic16(lop_and_or(r2 >> psh, 0x00030003u, kMagic16));
+        const uint32_t a3 = hsub_magic16(lop_and_or(r2 >> (psh + 8), 0x00030003u, kMagic16));
 #pragma unroll
-        for (int t = 0; t < HN; ++t) mma_bf16_16816(o[mt][t], a0, a1, a2, a3, bf[t][0], bf[t][1]);
+        for (int t = 0; t < HN; ++t) mma_f16_16816(o[mt][t], a0, a1, a2, a3, bf[t][0], bf[t][1]);
       }
     }
   }
@@ -606,7 +618,10 @@ static int launch_decode_t(const DecodeArgs& a, cudaStream_t s) {
   if (rc != ROLAQ_OK) return rc;
   rc = map_rows(&mr, a.cache.rope, CU_TENSOR_MAP_DATA_TYPE_UINT16, DR, a.cache.num_slots, DR * 2, kPage);
   if (rc != ROLAQ_OK) return rc;
-  cudaFuncSetAttribute(decode_kernel<D, DR, H>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+  static const bool attr_ok =
+      cudaFuncSetAttribute(decode_kernel<D, DR, H>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM) ==
+      cudaSuccess;
+  if (!attr_ok) return ROLAQ_ECUDA;
   dim3 grid(a.num_splits + 1, a.batch);
   decode_kernel<D, DR, H><<<grid, kDecodeThreads, C::SMEM, s>>>(mc, mr, a);
   return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;

@@ -374,11 +374,18 @@ int launch_writer(const uint16_t* x, int64_t ldx, const uint16_t* w, const Write
   if (rc != ROLAQ_OK) return rc;
   const int64_t tiles = ((args.n + kTileM - 1) / kTileM) * (d / kTileN);
   const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
+  // The attribute is set once per process (and per kernel), not on every launch, so
+  // that launches can be captured into CUDA graphs without extra API calls.
+  static const bool attr_plain =
+      cudaFuncSetAttribute(writer_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kWriterSmem) ==
+      cudaSuccess;
+  static const bool attr_codec =
+      cudaFuncSetAttribute(writer_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kWriterSmem) ==
+      cudaSuccess;
+  if (!(plain ? attr_plain : attr_codec)) return ROLAQ_ECUDA;
   if (plain) {
-    cudaFuncSetAttribute(writer_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kWriterSmem);
     writer_kernel<true><<<grid, kWriterThreads, kWriterSmem, stream>>>(mx, mw, args);
   } else {
-    cudaFuncSetAttribute(writer_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kWriterSmem);
     writer_kernel<false><<<grid, kWriterThreads, kWriterSmem, stream>>>(mx, mw, args);
   }
   return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;

@@ -1,0 +1,175 @@
+"""Reference-facing entry points on the GPU: the serving writer plugin through the
+pool, the reader, the HF quantizer API and the loader's read-rotation fold."""
+
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_helpers import bits, cosine, oracle_scalars
+from mla_kv_quant_b200 import ops, synth
+from mla_kv_quant_b200.mla_fused_writer import try_fast_decode_store
+from mla_kv_quant_b200.mla_packed_decode import packed_mla_decode_gf_fwd, prepare_gf_splits
+from mla_kv_quant_b200.pool import PackedLatentPool
+from mla_kv_quant_b200.quantizer import LearnedRotationQuantizer, rotate_quantize
+from mla_kv_quant_b200.rolaq_mla import fold_read_rotation
+from oracle import decode as odecode
+from oracle import writer as owriter
+
+pytestmark = pytest.mark.gpu
+
+
+def _oracle_pool(pool, li):
+    p = owriter.Pool(pool.size, pool.kv_lora_rank, pool.qk_rope_head_dim, pool._max_reqs, pool._win_p, pool._win_r)
+    p.codes = pool.c_codes[li].cpu().numpy()
+    p.params = pool.c_params[li].cpu().numpy()
+    p.rope = bits(pool.rope_buf[li])
+    p.hp = bits(pool.hp_c[li])
+    p.rows = pool.hp_row_of_slot.cpu().numpy()
+    p.owners = pool.hp_owner_of_row.cpu().numpy()
+    return p
+
+
+def test_decode_steps_through_pool_plugin(monkeypatch):
+    """Prefill 3 requests, then 40 decode steps through try_fast_decode_store (the
+    recent window wraps twice); the pool must equal the oracle's after every step and
+    the reader must match the oracle decode at the end."""
+    monkeypatch.setenv("SGLANG_ROLAQ_MLA_FUSED_DECODE_WRITE", "1")
+    layers, d, dr, h = 2, 512, 64, 16
+    rot = {i: synth.rotation(d, 100 + i) for i in range(layers)}
+    params = [(0.8, synth.signal_gain(0.8)), None]  # layer 1 falls back to the Lloyd-Max defaults
+    pool = PackedLatentPool(64 * 24, layers, max_reqs=4, rotations=rot, quantizer_params=params)
+    g = torch.Generator().manual_seed(0)
+    pages = (torch.randperm(23, generator=g) + 1).to(torch.int32)
+    pt = pages[:21].reshape(3, 7).cuda()
+    lens = [5, 100, 300]
+    oracle = [_oracle_pool(pool, li) for li in range(layers)]
+
+    def slot_of(b, p):
+        return int(pt[b, p // 64]) * 64 + p % 64
+
+    def write(li, c_kv, k_pe, slots, seq, req, positions, decode):
+        pool.set_window_meta(decode, seq, req)
+        if decode:
+            assert try_fast_decode_store(pool, li, slots, c_kv, k_pe)
+        else:
+            pool.set_kv_buffer(li, slots, c_kv, k_pe, positions=positions)
+        codec = pool.codec(li)
+        # the oracle codec runs on the kernel's own FP32 rotation (shared MMA order)
+        gpu_rot = torch.empty(c_kv.shape[0], d, device="cuda")
+        ops.rotate_rows(c_kv, pool.write_rotation_t(li), out_f32=gpu_rot)
+        owriter.write(oracle[li], gpu_rot.cpu().numpy(), bits(k_pe), slots.cpu().numpy(), seq.cpu().numpy(),
+                      req.cpu().numpy(), *oracle_scalars(codec)[:2],
+                      positions=None if positions is None else positions.cpu().numpy())
+
+    # prefill
+    for b, L in enumerate(lens):
+        for li in range(layers):
+            x = synth.latents(L, d, seed=10 * b + li, device="cuda")
+            pe = synth.normal_bf16((L, dr), seed=10 * b + li + 5, device="cuda")
+            slots = torch.tensor([slot_of(b, p) for p in range(L)], device="cuda")
+            write(li, x, pe, slots, torch.full((L,), L, dtype=torch.int32, device="cuda"),
+                  torch.full((L,), b, dtype=torch.int64, device="cuda"), torch.arange(L, device="cuda"), False)
+    # decode steps
+    for step in range(40):
+        lens = [L + 1 for L in lens]
+        slots = torch.tensor([slot_of(b, L - 1) for b, L in enumerate(lens)], device="cuda")
+        seq = torch.tensor(lens, dtype=torch.int32, device="cuda")
+        req = torch.arange(3, device="cuda")
+        for li in range(layers):
+            x = synth.latents(3, d, seed=1000 + 7 * step + li, device="cuda")
+            pe = synth.normal_bf16((3, dr), seed=2000 + step + li, device="cuda")
+            write(li, x, pe, slots, seq, req, None, True)
+    torch.cuda.synchronize()
+    for li in range(layers):
+        got = _oracle_pool(pool, li)
+        for name in ("codes", "params", "rope", "hp", "rows", "owners"):
+            assert np.array_equal(getattr(got, name), getattr(oracle[li], name)), (li, name)
+    # reader through the plugin entry point, with caller-provided scratch
+    q = synth.normal_bf16((3, h, d + dr), seed=77, device="cuda")
+    splits = torch.tensor([4, 4, 4], dtype=torch.int32, device="cuda")
+    quant, merge = torch.empty_like(splits), torch.empty_like(splits)
+    prepare_gf_splits(splits, quant, merge)
+    ns = int(quant.max())
+    out = packed_mla_decode_gf_fwd(q, pool, 1, pt, torch.tensor(lens, dtype=torch.int32, device="cuda"),
+                                   1 / np.sqrt(192), ns, attn_logits=torch.empty(3, h, ns + 1, d, device="cuda"),
+                                   attn_lse=torch.empty(3, h, ns + 1, device="cuda"))
+    torch.cuda.synchronize()
+    ref, _ = odecode.decode(oracle[1], bits(q), pt.cpu().numpy(), lens, 1 / np.sqrt(192))
+    for b in range(3):
+        o = out[b].float().cpu().numpy()
+        half_ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(ref[b]), 1e-30))) - 8)
+        assert np.max(np.abs(o - ref[b]) - half_ulp) <= 2e-2 and cosine(o, ref[b]) >= 0.9995
+
+
+def test_try_fast_decode_store_guards():
+    pool = PackedLatentPool(64 * 2, 1, rotations={0: synth.rotation(512, 1)})
+    x = synth.latents(2, 512, seed=1, device="cuda")
+    pe = synth.normal_bf16((2, 64), seed=2, device="cuda")
+    loc = torch.tensor([1, 2], device="cuda")
+    assert not try_fast_decode_store(pool, 0, loc, x, pe)  # no window metadata
+    pool.set_window_meta(False, torch.tensor([3, 3], device="cuda"), torch.tensor([0, 0], device="cuda"))
+    assert not try_fast_decode_store(pool, 0, loc, x, pe)  # prefill is not the decode writer's job
+    pool.set_window_meta(True, torch.tensor([3], device="cuda"), torch.tensor([0, 0], device="cuda"))
+    assert not try_fast_decode_store(pool, 0, loc, x, pe)  # metadata does not match the rows
+    pool.set_window_meta(True, torch.tensor([3, 4], device="cuda"), torch.tensor([0, 1], device="cuda"))
+    pool._audit_budget = 1
+    assert not try_fast_decode_store(pool, 0, loc, x, pe)
+    pool._audit_budget = 0
+    assert try_fast_decode_store(pool, 0, loc, x, pe)
+
+
+@pytest.mark.parametrize("d", [512, 256])
+def test_rotate_quantize_matches_reference_golden(golden_dir, d):
+    z = np.load(golden_dir / "rotate.npz")
+    lat = torch.from_numpy(z[f"lat{d}"].view(np.int16)).view(torch.bfloat16).reshape(1, -1, d).cuda()
+    r = torch.from_numpy(z[f"r{d}"])
+    t, g = z[f"tg{d}"]
+    for key, mask in ((f"out_plain{d}", None), (f"out_masked{d}", torch.from_numpy(z[f"mask{d}"]))):
+        ref = torch.from_numpy(z[key].view(np.int16)).view(torch.bfloat16).float().numpy().reshape(-1, d)
+        out = rotate_quantize(lat, r, 128, "oscar_lloyd", torch.tensor(t, dtype=torch.float32),
+                              torch.tensor(g, dtype=torch.float32), high_precision_mask=mask)
+        o = out.float().cpu().numpy().reshape(-1, d)
+        assert np.mean(o == ref) >= 0.97
+        assert np.max(np.abs(o - ref)) <= 2e-2 * max(1.0, np.abs(ref).max())
+        assert cosine(o, ref) >= 0.9995
+
+
+def test_learned_quantizer_matches_reference_golden(golden_dir):
+    z = np.load(golden_dir / "artifact.npz")
+    ref_json = json.loads((golden_dir / "artifact.json").read_text())
+    q = LearnedRotationQuantizer(golden_dir / "artifact_d256")
+    lat = torch.from_numpy(z["lat"].view(np.int16)).view(torch.bfloat16).cuda()
+
+    def cmp(out, key):
+        ref = torch.from_numpy(z[key].view(np.int16)).view(torch.bfloat16).float().numpy()
+        o = out.float().cpu().numpy()
+        assert o.shape == ref.shape
+        assert np.mean(o == ref) >= 0.97 and cosine(o, ref) >= 0.9995
+
+    cmp(q.quantize_layer(lat, 0, "nope"), "q0")
+    cmp(q.quantize_layer(lat, 1, "nope"), "q1")
+    cmp(q.quantize_layer(lat[:, -1:], 1, "nope"), "q1_decode")
+    mask = torch.zeros(40, dtype=torch.bool)
+    mask[:4] = True
+    mask[-16:] = True
+    q.high_precision_mask = mask
+    cmp(q.quantize_layer(lat, 0, "nope"), "q0_masked")
+    assert q.layer_calls == ref_json["layer_calls"]
+    assert q.call_count == ref_json["call_count"] and q.element_count == ref_json["element_count"]
+    assert [list(s) for s in q.first_shapes] == ref_json["first_shapes"]
+
+
+def test_fold_read_rotation_matches_reference_golden(golden_dir):
+    z = np.load(golden_dir / "artifact.npz")
+    w = torch.from_numpy(z["w"].view(np.int16)).view(torch.bfloat16)
+    ref = torch.from_numpy(z["w_folded1"].view(np.int16)).view(torch.bfloat16).float()
+    out_cpu = fold_read_rotation(w, 1, golden_dir / "artifact_d256")
+    out_gpu = fold_read_rotation(w.cuda(), 1, golden_dir / "artifact_d256")
+    assert out_cpu.device.type == "cpu" and out_gpu.is_cuda
+    assert torch.equal(out_cpu, out_gpu.cpu())
+    diff = (out_cpu.float() - ref).abs()
+    # accumulation order only: identical except one-ulp BF16 rounding flips
+    assert (diff == 0).float().mean() >= 0.97
+    assert torch.all(diff <= ref.abs() * 2 ** -7 + 1e-6)
