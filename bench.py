@@ -145,14 +145,18 @@ def build_state(dev, batch, ctx, seed):
     return pool, pt, pages
 
 
-def fill_cache(pool, pt, batch, ctx, dev, seed, writer_timing=None):
+def fill_cache(pool, pt, batch, ctx, dev, seed):
+    fill_cache_layers(pool, pt, batch, ctx, dev, seed, LAYERS)
+
+
+def fill_cache_layers(pool, pt, batch, ctx, dev, seed, layers):
     """Prefill every layer: 8 requests x ctx rows per writer launch (config-1 shape)."""
     from mla_kv_quant_b200 import ops, synth
 
     scale = synth.channel_scale(D, 77, dev)
     chunk = 8
     pos = torch.arange(ctx, device=dev)
-    for li in range(LAYERS):
+    for li in range(layers):
         rt = pool.write_rotation_t(li)
         codec = pool.codec(li)
         view = pool.layer_view(li)
@@ -266,11 +270,13 @@ def run_ours(args, rank, world, dev):
     torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev) as clk:
+        torch.cuda.nvtx.range_push("timed")  # `ncu --nvtx --nvtx-include timed/` captures exactly this
         s.record()
         for _ in range(args.steps):
             graph.replay()
         e.record()
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     if world > 1:
         torch.distributed.barrier()
     step_s = s.elapsed_time(e) / 1e3 / args.steps
@@ -429,8 +435,55 @@ def run_reference(args, rank, world):
     }
 
 
+def profile_layer(args, what):
+    """One layer of the benchmark shape for ncu captures (~0.3 GB on the device):
+    fill the cache with the config-1 writer, then run 3 decode (or writer) launches."""
+    from mla_kv_quant_b200 import ops, synth
+    from mla_kv_quant_b200.pool import PackedLatentPool
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    batch, ctx = args.batch, args.ctx
+    pt, num_slots = synth.page_table(batch, ctx, seed=4, device=dev)
+    pool = PackedLatentPool(num_slots, 1, D, DR, max_reqs=batch, sink=SINK, recent=RECENT, device=dev,
+                            rotations={0: synth.rotation(D, 1000)}, quantizer_params=[(0.85, synth.signal_gain(0.85))])
+    fill_cache_layers(pool, pt, batch, ctx, dev, seed=0, layers=1)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    times = []
+    if what == "decode":
+        splits = args.splits or ops.default_num_splits(batch, ctx)
+        q = synth.normal_bf16((batch, HEADS, D + DR), 3, dev)
+        sl = torch.full((batch,), ctx, dtype=torch.int32, device=dev)
+        po = torch.empty(batch, HEADS, splits + 1, D, device=dev)
+        pl = torch.empty(batch, HEADS, splits + 1, device=dev)
+        out = torch.empty(batch, HEADS, D, dtype=torch.bfloat16, device=dev)
+        for _ in range(3):
+            ev[0].record()
+            ops.packed_decode(q, pool.layer_view(0), pt, sl, 1 / math.sqrt(192.0), splits, po, pl, out)
+            ev[1].record()
+            torch.cuda.synchronize()
+            times.append(ev[0].elapsed_time(ev[1]) * 1e3)
+        print(json.dumps({"mode": "decode-layer", "us": times, "splits": splits,
+                          "algorithmic_bytes": decode_bytes(batch, ctx)}))
+    else:
+        n = 8 * ctx
+        x = synth.latents(n, D, 5, dev)
+        pe = synth.normal_bf16((n, DR), 6, dev)
+        slots = torch.arange(64, 64 + n, device=dev, dtype=torch.int64)
+        for _ in range(3):
+            ev[0].record()
+            ops.fused_write(x, pe, slots, pool.write_rotation_t(0), pool.codec(0), pool.layer_view(0))
+            ev[1].record()
+            torch.cuda.synchronize()
+            times.append(ev[0].elapsed_time(ev[1]) * 1e3)
+        print(json.dumps({"mode": "writer-layer", "us": times, "rows": n, "algorithmic_bytes": writer_bytes(n),
+                          "flops": 2.0 * n * D * D}))
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--mode", choices=["step", "decode-layer", "writer-layer"], default="step",
+                    help="step: the benchmark; *-layer: one layer, 3 launches (for ncu captures)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
@@ -447,6 +500,9 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.mode != "step":
+        profile_layer(args, args.mode.split("-")[0])
+        return 0
 
     if args.impl == "reference":
         if world > 1:
