@@ -157,6 +157,142 @@ __device__ void window_split(const DecodeArgs& a, uint8_t* smem, int b, int L) {
   }
 }
 
+// The window split on its own (used with the tcgen05 INT2 kernel): grid = (batch, H / 4),
+// four heads per CTA, one warp per head.  Same arithmetic as window_split (the q.k dot
+// product runs as four interleaved partial sums); the rows are gathered once per row
+// (lookups by one thread, elements by a warp, coalesced) into shared rows padded to an odd
+// stride, so that a lane per row reads them without bank conflicts.
+constexpr int kWinHeads = 4;
+template <int D, int DR>
+constexpr size_t window_rows_smem() {
+  return (size_t(kMaxWindow) * (D + DR + 1) + size_t(kWinHeads) * (D + DR) + size_t(kWinHeads) * kMaxWindow) * 4;
+}
+
+template <int D, int DR, int H>
+__global__ void __launch_bounds__(kWinHeads * 32) window_rows_kernel(const DecodeArgs a) {
+  constexpr int KW = D + DR, KP = KW + 1;
+  extern __shared__ float wsm[];
+  float* kw = wsm;                        // [kMaxWindow][KP]
+  float* qf = kw + kMaxWindow * KP;       // [kWinHeads][KW]
+  float* pr = qf + kWinHeads * KW;        // [kWinHeads][kMaxWindow]
+  __shared__ float wm[kWinHeads], wl[kWinHeads];
+  __shared__ int64_t rslot[kMaxWindow];
+  __shared__ int64_t rrow[kMaxWindow];
+  const int b = blockIdx.x, h0 = blockIdx.y * kWinHeads;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  int L = a.seq_lens[b];
+  if (L < 0) L = 0;
+  if (L > a.max_pages * kPage) L = a.max_pages * kPage;
+  const int P = a.cache.sink, W = a.cache.recent;
+  const int lo = min(P, L);
+  const int hs = max(lo, L - W);
+  int rs = 0, re = L;
+  if (a.token_range != nullptr) {
+    rs = max(0, a.token_range[2 * b]);
+    re = min(L, a.token_range[2 * b + 1]);
+  }
+  const int s1 = min(max(rs, 0), lo), e1 = max(min(re, lo), s1);
+  const int s2 = min(max(rs, hs), L), e2 = max(min(re, L), s2);
+  const int n1 = e1 - s1;
+  const int nw = n1 + (e2 - s2);  // <= sink + recent <= kMaxWindow (checked by the host)
+  for (int idx = tid; idx < kWinHeads * KW; idx += blockDim.x) {
+    const int h = idx / KW, e = idx % KW;
+    qf[idx] = bf16f(a.q[b * a.q_sb + (h0 + h) * a.q_sh + e]);
+  }
+  if (tid < nw) {  // per row: slot and the ring row that holds it (if any)
+    const int pos = tid < n1 ? s1 + tid : s2 + (tid - n1);
+    const int64_t page = a.page_table[b * a.pt_stride + pos / kPage];
+    int64_t slot = -1, r = -1;
+    if (page >= 0 && (page + 1) * kPage <= a.cache.num_slots) {
+      slot = page * kPage + pos % kPage;
+      r = a.cache.rows ? a.cache.rows[slot] : -1;
+      if (!(r >= 0 && r < a.cache.num_ring_rows && a.cache.owners[r] == slot)) r = -1;
+    } else {
+      report(a.err, ROLAQ_DEV_BAD_PAGE);
+    }
+    rslot[tid] = slot;
+    rrow[tid] = r;
+  }
+  __syncthreads();
+  for (int p = warp; p < nw; p += kWinHeads) {
+    const int64_t slot = rslot[p], r = rrow[p];
+    float* dst = kw + p * KP;
+    if (slot < 0) {
+      for (int e = lane; e < KW; e += 32) dst[e] = 0.f;
+      continue;
+    }
+    if (r >= 0) {
+      for (int e = lane; e < D; e += 32) dst[e] = bf16f(a.cache.hp[r * D + e]);
+    } else {
+      for (int e = lane; e < D; e += 32) {
+        const uint32_t c = (a.cache.codes[slot * (D / 4) + e / 4] >> (2 * (e % 4))) & 3u;
+        const float2 sz = reinterpret_cast<const float2*>(a.cache.params)[slot * (D / 128) + e / 128];
+        dst[e] = __fmul_rn(__fsub_rn(static_cast<float>(c), sz.y), sz.x);
+      }
+    }
+    for (int e = lane; e < DR; e += 32) dst[D + e] = bf16f(a.cache.rope[slot * DR + e]);
+  }
+  __syncthreads();
+  {  // warp = head, lane = row
+    const int h = warp;
+    float sc = -INFINITY;
+    if (lane < nw) {  // four interleaved partial sums (KW is a multiple of 4)
+      const float* k = kw + lane * KP;
+      const float* qh = qf + h * KW;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
+      for (int e = 0; e < KW; e += 4) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) acc[u] = fmaf(qh[e + u], k[e + u], acc[u]);
+      }
+      sc = ((acc[0] + acc[1]) + (acc[2] + acc[3])) * a.sm_scale;
+    }
+    float m = sc;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    const float ex = lane < nw ? __expf(sc - m) : 0.f;
+    pr[h * kMaxWindow + lane] = ex;
+    __syncwarp();
+    if (lane == 0) {  // the sum in row order, as window_split
+      float l = 0.f;
+      for (int p = 0; p < nw; ++p) l += pr[h * kMaxWindow + p];
+      wm[h] = m;
+      wl[h] = l;
+    }
+  }
+  __syncthreads();
+  const int S = a.num_splits + 1;
+  static_assert(D % (kWinHeads * 32) == 0, "latent elements per thread");
+  constexpr int JT = D / (kWinHeads * 32);  // elements per thread, for all kWinHeads heads
+  float o[kWinHeads][JT];
+#pragma unroll
+  for (int h = 0; h < kWinHeads; ++h)
+#pragma unroll
+    for (int c = 0; c < JT; ++c) o[h][c] = 0.f;
+  for (int p = 0; p < nw; ++p) {
+    float kv[JT];
+#pragma unroll
+    for (int c = 0; c < JT; ++c) kv[c] = kw[p * KP + tid + c * kWinHeads * 32];
+#pragma unroll
+    for (int h = 0; h < kWinHeads; ++h) {
+      const float w = pr[h * kMaxWindow + p];
+#pragma unroll
+      for (int c = 0; c < JT; ++c) o[h][c] = fmaf(w, kv[c], o[h][c]);
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < kWinHeads; ++h) {
+    const int64_t row = (static_cast<int64_t>(b) * H + h0 + h) * S + a.num_splits;
+#pragma unroll
+    for (int c = 0; c < JT; ++c)
+      a.part_o[row * D + tid + c * kWinHeads * 32] = nw > 0 ? o[h][c] / wl[h] : 0.f;
+  }
+  if (tid < kWinHeads) {
+    const int64_t row = (static_cast<int64_t>(b) * H + h0 + tid) * S + a.num_splits;
+    a.part_lse[row] = nw > 0 ? wm[tid] + logf(wl[tid]) : -INFINITY;
+  }
+}
+
 template <int D, int DR, int H>
 __global__ void __launch_bounds__(kDecodeThreads, 2)
     decode_kernel(const __grid_constant__ CUtensorMap tm_codes, const __grid_constant__ CUtensorMap tm_rope,
@@ -627,8 +763,29 @@ static int launch_decode_t(const DecodeArgs& a, cudaStream_t s) {
   return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;
 }
 
+template <int D, int DR, int H>
+static int launch_window_t(const DecodeArgs& a, cudaStream_t s) {
+  static_assert(H % kWinHeads == 0, "heads per window CTA");
+  constexpr size_t smem = window_rows_smem<D, DR>();
+  static const bool attr_ok =
+      cudaFuncSetAttribute(window_rows_kernel<D, DR, H>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ==
+      cudaSuccess;
+  if (!attr_ok) return ROLAQ_ECUDA;
+  window_rows_kernel<D, DR, H><<<dim3(a.batch, H / kWinHeads), kWinHeads * 32, smem, s>>>(a);
+  return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;
+}
+
+bool decode_tc_supported(const DecodeArgs& a, int heads);
+int launch_decode_tc(const DecodeArgs& a, cudaStream_t s);
+
 int launch_decode(const DecodeArgs& a, int heads, cudaStream_t s) {
   const int d = a.cache.latent_dim, dr = a.cache.rope_dim;
+  if (decode_tc_supported(a, heads)) {
+    // tcgen05 kernel for the INT2 splits, the window split on its own
+    int rc = launch_decode_tc(a, s);
+    if (rc != ROLAQ_OK) return rc;
+    return launch_window_t<512, 64, 16>(a, s);
+  }
   if (d == 512 && dr == 64 && heads == 16) return launch_decode_t<512, 64, 16>(a, s);
   if (d == 512 && dr == 64 && heads == 8) return launch_decode_t<512, 64, 8>(a, s);
   if (d == 256 && dr == 32 && heads == 40) return launch_decode_t<256, 32, 40>(a, s);

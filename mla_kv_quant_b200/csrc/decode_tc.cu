@@ -1,0 +1,703 @@
+// Packed-INT2 MLA decode attention on tcgen05 tensor cores (sm_100a), D = 512, Dr = 64,
+// H = 16 (DeepSeek-V2-Lite / Moonlight shape).
+//
+// Reference behaviour: upstream packed_mla_decode_gf_fwd called at
+// deployment/patches/rolaq_sglang.patch:51-111; queries in the rotated frame
+// (deployment/sglang/srt/mem_cache/rolaq_mla.py:56-71).
+//
+// One CTA per (request, KV split) walks its split in tiles of 128 tokens (two 64-slot
+// pages).  The dequantised latent of token t in group g is s_tg (c_te - z_tg); the
+// kernel never forms it:
+//   q . c_hat = sum_g s_g (q_g . c - z_g sum(q_g))          (scores)
+//   sum_t P_t c_hat_t = sum_g [sum_t (P_t s_tg) c_t - sum_t (P_t s_tg) z_tg]   (PV)
+// Codes enter the tensor cores as FP8 E4M3 bytes holding c or 4c: the E4M3 patterns
+// 0..15 are exactly p * 2^-9 (subnormals continue linearly into the first normal
+// binade), so `w & 0x03030303` and `w & 0x0C0C0C0C` turn a packed word into four
+// exact operands with one AND each.  Elements stored as 4c get a query weight of 1/4
+// (QK) and an output weight of 1/4 (PV).
+//
+// Per tile:
+//   * 16 token warps, four threads per token (thread k: codes of group k, softmax of
+//     heads 4k..4k+3) expand the codes into TMEM (A of QK^T, lane = token) and into an
+//     MN-major smem tile (A of PV, row = token);
+//   * QK^T = kind::f8f6f4, M = 128 tokens, N = 32 (16 heads x {hi, lo} E4M3 terms of the
+//     query, exact for BF16 after a per-head power-of-two scale), + the rope part in
+//     kind::f16 with k_pe staged by TMA;
+//   * the token threads turn scores into P = 2^(s - m_ref) against a reference max that
+//     moves only when a tile max exceeds it by more than kTau (lazy rescaling), and
+//     write P' = P s_g E_g (E_g a per-group power of two that moves only when the group
+//     scale outgrows it) as two E4M3 terms;
+//   * PV = kind::f8f6f4 (M = 128 latent elements of a group, N = 32, K = 128 tokens)
+//     accumulates straight into a TMEM O accumulator across all tiles.
+// When m_ref or E_g moves, each token warp rescales the O columns of its own heads in
+// TMEM (lane quarter = its tokens' quarter) and, at the end, writes those columns.  An
+// issuer warp does all MMA issue, the k_pe TMA and L2 prefetch, driven by mbarriers, so
+// the token warps never wait on one another's issue work: QK^T(i+1) is issued as soon
+// as its codes are in TMEM and PV(i) as soon as P'(i) is in shared memory.
+#include "kernels.cuh"
+
+namespace rolaq {
+namespace tc {
+
+constexpr int D = 512, DR = 64, H = 16, NG = 4;
+constexpr int TILE = 128, PAGE = 64;
+constexpr int NTOK_WARPS = 16;  // + one issuer warp (17 warps: at most 5 per SM sub-partition -> 96 registers)
+constexpr int TOK_THREADS = NTOK_WARPS * 32;
+constexpr int THREADS = TOK_THREADS + 32;
+// P' = 2^(s - m_ref) s_g E_g < 2^kTau * kEMax = 362 stays inside E4M3 (448).
+constexpr float kTau = 4.5f;    // m_ref moves when a tile max exceeds it by more than this (log2 units)
+constexpr float kEMax = 16.f;   // E_g moves when max_t s_tg * E_g reaches this (set to [4, 8))
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// ---- shared memory (offsets from a 1024-byte aligned base) ---------------------------------
+constexpr int KPE_STAGE = TILE * DR * 2;  // 16 KB: k_pe of the tile, K-major SW128 (TMA)
+constexpr int PVA_GROUP = TILE * 128;     // 16 KB: 128 tokens x 128 B, MN-major SW128
+constexpr int PVA_BUF = NG * PVA_GROUP;   // 64 KB
+constexpr int QB_GROUP = 32 * 128;        // 4 KB: 32 query rows x 128 B, K-major SW128
+constexpr int QPE_BYTES = H * DR * 2;     // 2 KB: 16 rows x 128 B, K-major SW128
+constexpr int PB_GROUP = TILE * 32;       // 4 KB: 128 tokens x 32 B, MN-major SW32
+constexpr int PB_BUF = NG * PB_GROUP;     // 16 KB
+constexpr int PAR_STAGE = TILE * NG * 2 * 4;  // 4 KB: (scale, zero) x 4 groups per token (bulk copy)
+constexpr int OFF_KPE = 0;
+constexpr int OFF_PVA = OFF_KPE + 2 * KPE_STAGE;
+constexpr int OFF_QB = OFF_PVA + 2 * PVA_BUF;
+constexpr int OFF_QPE = OFF_QB + NG * QB_GROUP;
+constexpr int OFF_PB = OFF_QPE + QPE_BYTES;
+constexpr int OFF_PAR = OFF_PB + 2 * PB_BUF;
+constexpr int OFF_F = OFF_PAR + 2 * PAR_STAGE;
+// float scratch
+constexpr int F_QSUM = 0;               // [NG][H]     sum of the query over the group
+constexpr int F_KINV = F_QSUM + NG * H;  // [H]         2^(9 - k_h)
+constexpr int F_HMAX = F_KINV + H;       // [2][H][4]   tile max per head and token quarter
+constexpr int F_GMAX = F_HMAX + 2 * H * 4;   // [2][NG][4]  tile max of s_g per token quarter
+constexpr int F_FINL = F_GMAX + 2 * NG * 4;  // [4][H]      sum P per token quarter
+constexpr int F_FINY = F_FINL + 4 * H;       // [4][NG][H]  sum P' z per token quarter
+constexpr int F_TOTAL = F_FINY + 4 * NG * H;
+constexpr int OFF_BAR = OFF_F + ((F_TOTAL * 4 + 15) / 16) * 16;
+constexpr int B_KPE = 0, B_QK = 2, B_PV = 3, B_AQK = 4, B_PREADY = 5, B_PAR = 6, N_BARS = 8;
+constexpr int OFF_TMEMSLOT = OFF_BAR + N_BARS * 8;
+constexpr size_t SMEM = size_t(OFF_TMEMSLOT) + 16 + 1024;
+static_assert(SMEM <= 227 * 1024, "shared memory budget");
+static_assert(kEMax * 22.7f < 448.f, "P' must stay below the largest E4M3 value");
+static_assert(F_HMAX % 4 == 0 && F_GMAX % 4 == 0 && F_QSUM % 4 == 0 && F_KINV % 4 == 0,
+              "float4 alignment of the scratch tables");
+
+// ---- TMEM columns ---------------------------------------------------------------------------
+constexpr uint32_t T_AQK = 0;    // 128 cols: FP8 codes of the tile (lane = token)
+constexpr uint32_t T_DQK = 128;  // 128 cols: QK^T, 32 per group: [k: hi heads 4k.., lo heads 4k..]
+constexpr uint32_t T_DPE = 256;  // 16 cols: rope scores
+constexpr uint32_t T_O = 384;    // 128 cols: O, 32 per group, same column order as T_DQK
+
+__device__ __forceinline__ uint32_t sw128(int row, int byte) {  // 128-byte rows, 1024-byte atoms
+  return static_cast<uint32_t>((row >> 3) * 1024 + (row & 7) * 128 + (((byte >> 4) ^ (row & 7)) << 4) +
+                               (byte & 15));
+}
+__device__ __forceinline__ uint32_t sw32(int row, int byte) {  // 32-byte rows, 256-byte atoms
+  return static_cast<uint32_t>((row >> 3) * 256 + (row & 7) * 32 + (((byte >> 4) ^ ((row >> 2) & 1)) << 4) +
+                               (byte & 15));
+}
+
+__device__ __forceinline__ float pow2i(int e) { return __int_as_float((e + 127) << 23); }
+
+// E_g for a tile whose largest group scale is gm >= 0: the power of two with gm * E in [4, 8).
+__device__ __forceinline__ float group_e(float gm) {
+  int eb = (__float_as_int(gm) >> 23) & 0xFF;
+  eb = min(max(eb, 29), 225);
+  return __int_as_float((256 - eb) << 23);
+}
+
+__device__ __forceinline__ float max4(float4 v) { return fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)); }
+
+// K index (position in a row of FP8 operand bytes) <-> element of the group; an involution.
+__device__ __forceinline__ int kperm(int w) { return (w & ~15) | ((w & 3) << 2) | ((w >> 2) & 3); }
+
+__global__ void __launch_bounds__(THREADS, 1)
+    decode_tc_kernel(const __grid_constant__ CUtensorMap tm_rope, const DecodeArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  float* F = reinterpret_cast<float*>(smem + OFF_F);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEMSLOT);
+
+  const int b = blockIdx.y, split = blockIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int S = a.num_splits + 1;  // the window split (index num_splits) is written by window_kernel
+  int L = a.seq_lens[b];
+  if (L < 0) L = 0;
+  if (L > a.max_pages * PAGE) {
+    if (tid == 0) report(a.err, ROLAQ_DEV_BAD_REQ);
+    L = a.max_pages * PAGE;
+  }
+  const int P = a.cache.sink, W = a.cache.recent;
+  int lo = min(P, L);
+  int hi = max(lo, L - W);
+  if (a.token_range != nullptr) {
+    lo = max(lo, a.token_range[2 * b]);
+    hi = max(lo, min(hi, a.token_range[2 * b + 1]));
+  }
+  const int first_page = lo / PAGE;
+  const int npages = hi > lo ? (hi - 1) / PAGE - first_page + 1 : 0;
+  const int pps = 2 * ((npages + 2 * a.num_splits - 1) / (2 * a.num_splits));
+  const int p0 = first_page + split * pps;
+  const int p1 = min(first_page + npages, p0 + pps);
+  if (p0 >= p1) {
+    for (int u = tid; u < H * D; u += blockDim.x) {
+      const int h = u / D, j = u % D;
+      a.part_o[((static_cast<int64_t>(b) * H + h) * S + split) * D + j] = 0.f;
+    }
+    if (tid < H) a.part_lse[(static_cast<int64_t>(b) * H + tid) * S + split] = -INFINITY;
+    return;
+  }
+  const int ntiles = (p1 - p0 + 1) / 2;
+
+  // Page ids are fetched ahead of use (page_raw: an unconditional load from a clamped
+  // index, so that nothing waits on it until it is used) and checked when used
+  // (page_of: absence is a property of the tile index, not of the loaded value).
+  auto page_raw = [&](int i, int half) -> int32_t {
+    return a.page_table[b * a.pt_stride + min(p0 + 2 * i + half, p1 - 1)];
+  };
+  auto page_of = [&](int i, int half, int32_t raw) -> int64_t {  // pool page; -1 absent, -2 out of range
+    if (p0 + 2 * i + half >= p1) return -1;
+    return (raw >= 0 && (static_cast<int64_t>(raw) + 1) * PAGE <= a.cache.num_slots) ? raw : -2;
+  };
+  // k_pe of tile i (page ids r0, r1) into stage i & 1 (elected thread)
+  auto issue_kpe = [&](int i, int32_t r0, int32_t r1) {
+    const int s = i & 1;
+    const int64_t pg0 = page_of(i, 0, r0), pg1 = page_of(i, 1, r1);
+    const uint32_t bytes = (pg0 >= 0 ? PAGE * DR * 2 : 0) + (pg1 >= 0 ? PAGE * DR * 2 : 0);
+    if (pg0 == -2 || pg1 == -2) report(a.err, ROLAQ_DEV_BAD_PAGE);
+    if (bytes == 0) {
+      mbar_arrive(&bars[B_KPE + s]);
+      return;
+    }
+    mbar_expect_tx(&bars[B_KPE + s], bytes);
+    uint8_t* st = smem + OFF_KPE + s * KPE_STAGE;
+    if (pg0 >= 0) tma_load_2d(st, &tm_rope, &bars[B_KPE + s], 0, static_cast<int32_t>(pg0 * PAGE));
+    if (pg1 >= 0)
+      tma_load_2d(st + PAGE * DR * 2, &tm_rope, &bars[B_KPE + s], 0, static_cast<int32_t>(pg1 * PAGE));
+  };
+  // (scale, zero) rows of tile i into params stage i & 1 (elected thread)
+  auto issue_params = [&](int i, int32_t r0, int32_t r1) {
+    const int s = i & 1;
+    const int64_t pg0 = page_of(i, 0, r0), pg1 = page_of(i, 1, r1);
+    const uint32_t bytes = (pg0 >= 0 ? PAR_STAGE / 2 : 0) + (pg1 >= 0 ? PAR_STAGE / 2 : 0);
+    if (bytes == 0) {
+      mbar_arrive(&bars[B_PAR + s]);
+      return;
+    }
+    mbar_expect_tx(&bars[B_PAR + s], bytes);
+    uint8_t* st = smem + OFF_PAR + s * PAR_STAGE;
+    if (pg0 >= 0) bulk_load(st, a.cache.params + pg0 * PAGE * NG * 2, PAR_STAGE / 2, &bars[B_PAR + s]);
+    if (pg1 >= 0) bulk_load(st + PAR_STAGE / 2, a.cache.params + pg1 * PAGE * NG * 2, PAR_STAGE / 2, &bars[B_PAR + s]);
+  };
+  auto prefetch_tile = [&](int i, int32_t r0, int32_t r1) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int64_t pg = page_of(i, half, half ? r1 : r0);
+      if (pg < 0) continue;
+      prefetch_l2(a.cache.codes + pg * PAGE * (D / 4), PAGE * (D / 4));
+      prefetch_l2(a.cache.params + pg * PAGE * NG * 2, PAGE * NG * 2 * 4);
+      prefetch_l2(a.cache.rope + pg * PAGE * DR, PAGE * DR * 2);
+    }
+  };
+
+  // ---- set-up ---------------------------------------------------------------------------
+  if (tid == 0) {
+    mbar_init(&bars[B_KPE], 1);
+    mbar_init(&bars[B_KPE + 1], 1);
+    mbar_init(&bars[B_PAR], 1);
+    mbar_init(&bars[B_PAR + 1], 1);
+    mbar_init(&bars[B_QK], 1);
+    mbar_init(&bars[B_PV], 1);
+    mbar_init(&bars[B_AQK], TOK_THREADS);
+    mbar_init(&bars[B_PREADY], TOK_THREADS);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  // queries: per-head scale 2^k_h, E4M3 hi/lo B tiles in the K order of the code bytes
+  // (odd elements weighted 1/4), group sums, rope rows
+  if (tid < TOK_THREADS) {
+    const int h = tid >> 5, part = lane;  // latent elements [16 * part, +16) of head h
+    const uint16_t* qh = a.q + b * a.q_sb + h * a.q_sh;
+    float v[16];
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const uint4 w = *reinterpret_cast<const uint4*>(qh + 16 * part + 8 * c);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        v[8 * c + 2 * k] = bf16_lo(ws[k]);
+        v[8 * c + 2 * k + 1] = bf16_hi(ws[k]);
+      }
+    }
+    float mx = 0.f, sum = 0.f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      mx = fmaxf(mx, fabsf(v[e]));
+      sum += v[e];
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+#pragma unroll
+    for (int o = 1; o <= 4; o <<= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);  // 8 parts per group
+    int ex = 0;
+    if (mx > 0.f) frexpf(mx, &ex);  // mx < 2^ex
+    ex = min(max(ex, -100), 100);
+    const int kh = 7 - ex;  // |q| * 2^kh < 128
+    const float qs = pow2i(kh);
+    if (part == 0) F[F_KINV + h] = pow2i(9 - kh);
+    const int g = part >> 3;
+    if ((part & 7) == 0) F[F_QSUM + g * H + h] = sum;
+    uint8_t* qb = smem + OFF_QB + g * QB_GROUP;
+    const int row_hi = 8 * (h >> 2) + (h & 3), row_lo = row_hi + 4;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const int kk = kperm(16 * (part & 7) + e);
+      const float x = v[e] * qs * ((e & 1) ? 0.25f : 1.f);
+      const uint32_t hq = f32x2_to_e4m3x2(x, 0.f) & 0xFFu;
+      const float hf = __low2float(e4m3x2_to_half2(hq));
+      const uint32_t lq = f32x2_to_e4m3x2((x - hf) * 16.f, 0.f) & 0xFFu;
+      qb[sw128(row_hi, kk)] = static_cast<uint8_t>(hq);
+      qb[sw128(row_lo, kk)] = static_cast<uint8_t>(lq);
+    }
+    if (part < 8) {  // rope part of the query: BF16 row of 64 into a K-major SW128 tile
+      const uint4 w = *reinterpret_cast<const uint4*>(qh + D + 8 * part);
+      *reinterpret_cast<uint4*>(smem + OFF_QPE + sw128(h, 16 * part)) = w;
+    }
+    fence_proxy_async();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool alive = true;
+  const uint32_t id_qk = idesc_e4m3(128, 32, 0, 0);
+  const uint32_t id_pe = idesc_bf16(128, 16);
+  const uint32_t id_pv = idesc_e4m3(128, 32, 1, 1);
+  auto issue_qk = [&](int i) {
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      const uint32_t qb = smem_u32(smem + OFF_QB + g * QB_GROUP);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        umma_f8_ts(tmem + T_DQK + 32 * g, tmem + T_AQK + 32 * g + 8 * kk, sw128_kmajor_desc(qb + 32 * kk), id_qk,
+                   kk > 0);
+    }
+    const uint32_t ka = smem_u32(smem + OFF_KPE + (i & 1) * KPE_STAGE);
+    const uint32_t kb = smem_u32(smem + OFF_QPE);
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk)
+      umma_bf16_ss(tmem + T_DPE, sw128_kmajor_desc(ka + 32 * kk), sw128_kmajor_desc(kb + 32 * kk), id_pe, kk > 0);
+    umma_commit(&bars[B_QK]);
+  };
+
+  auto issue_pv = [&](int i) {
+    const int s = i & 1;
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      const uint32_t pa = smem_u32(smem + OFF_PVA + s * PVA_BUF + g * PVA_GROUP);
+      const uint32_t pbb = smem_u32(smem + OFF_PB + s * PB_BUF + g * PB_GROUP);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        umma_f8_ss(tmem + T_O + 32 * g, mn_major_desc(pa + 4096 * kk, 128), mn_major_desc(pbb + 1024 * kk, 32),
+                   id_pv, (i > 0 || kk > 0) ? 1u : 0u);
+    }
+    umma_commit(&bars[B_PV]);
+  };
+
+  if (warp < NTOK_WARPS) {
+    // ---- token warps ------------------------------------------------------------------------
+    const int q4 = warp & 3, k = warp >> 2;
+    const int t = 32 * q4 + lane;  // token of the tile (TMEM lane)
+    const uint32_t lane_base = static_cast<uint32_t>(32 * q4) << 16;
+    const float sl2 = a.sm_scale * kLog2e;
+    float m_ref[4], lsum[4], y[NG][4], E[NG];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      m_ref[j] = -INFINITY;
+      lsum[j] = 0.f;
+#pragma unroll
+      for (int g = 0; g < NG; ++g) y[g][j] = 0.f;
+    }
+#pragma unroll
+    for (int g = 0; g < NG; ++g) E[g] = 0.f;
+
+    // next tile's codes of group k (32 B)
+    uint4 cw0, cw1;
+    bool ok_next = false;
+    auto load_tile = [&](int i, int32_t raw) {
+      // Codes of absent or masked tokens are never weighted (P' = 0, score discarded), so
+      // they are loaded from slot 0 (padding) instead of being zeroed: no select on the load.
+      const int64_t pg = page_of(i, t >> 6, raw);
+      const int pos = (p0 + 2 * i) * PAGE + t;
+      ok_next = pg >= 0 && pos >= lo && pos < hi;
+      const int64_t slot = pg >= 0 ? pg * PAGE + (t & 63) : 0;
+      const uint4* src = reinterpret_cast<const uint4*>(a.cache.codes + slot * (D / 4) + 32 * k);
+      cw0 = src[0];
+      cw1 = src[1];
+    };
+    auto expand = [&](uint32_t(&r)[32]) {
+      const uint32_t wd[8] = {cw0.x, cw0.y, cw0.z, cw0.w, cw1.x, cw1.y, cw1.z, cw1.w};
+#pragma unroll
+      for (int kq = 0; kq < 8; ++kq) {
+        const uint32_t w = wd[kq], w4 = wd[kq] >> 4;
+        r[4 * kq + 0] = w & 0x03030303u;   // c of element 16kq + 4b + 0, byte b
+        r[4 * kq + 1] = w & 0x0C0C0C0Cu;   // 4c of element 16kq + 4b + 1
+        r[4 * kq + 2] = w4 & 0x03030303u;  // c of element 16kq + 4b + 2
+        r[4 * kq + 3] = w4 & 0x0C0C0C0Cu;  // 4c of element 16kq + 4b + 3
+      }
+    };
+    auto store_pva = [&](int buf, const uint32_t(&r)[32]) {
+      uint8_t* base = smem + OFF_PVA + buf * PVA_BUF + k * PVA_GROUP;
+#pragma unroll
+      for (int kq = 0; kq < 8; ++kq)
+        *reinterpret_cast<uint4*>(base + sw128(t, 16 * kq)) =
+            make_uint4(r[4 * kq], r[4 * kq + 1], r[4 * kq + 2], r[4 * kq + 3]);
+    };
+    // prologue: tile 0 into TMEM and PV-A buffer 0, QK^T(0)
+    load_tile(0, page_raw(0, t >> 6));
+    int32_t pg_ahead = page_raw(1, t >> 6);  // page id of tile i + 2 (in the loop)
+    {
+      uint32_t r[32];
+      expand(r);
+      tmem_st32(tmem + lane_base + T_AQK + 32 * k, r);
+      store_pva(0, r);
+      tmem_wait_st();
+    }
+    fence_proxy_async();
+    tc_fence_before();
+    mbar_arrive(&bars[B_AQK]);  // A of QK^T(0) is in TMEM
+    bool ok = ok_next;
+    if (ntiles > 1) load_tile(1, pg_ahead);
+    pg_ahead = page_raw(2, t >> 6);
+
+    for (int i = 0; i < ntiles; ++i) {
+      const int s = i & 1;
+      // -- 1. scores of tile i --
+      if (alive) alive = mbar_wait(&bars[B_QK], i & 1, a.err);
+      __syncwarp();
+      tc_fence_after();
+      if (alive) alive = mbar_wait(&bars[B_PAR + s], (i >> 1) & 1, a.err);
+      float sc[NG], zz[NG];
+      {
+        const float4* pr = reinterpret_cast<const float4*>(smem + OFF_PAR + s * PAR_STAGE + t * (NG * 2 * 4));
+        const float4 p0v = pr[0], p1v = pr[1];
+        sc[0] = p0v.x;
+        zz[0] = p0v.y;
+        sc[1] = p0v.z;
+        zz[1] = p0v.w;
+        sc[2] = p1v.x;
+        zz[2] = p1v.y;
+        sc[3] = p1v.z;
+        zz[3] = p1v.w;
+      }
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {  // slots outside the range may hold anything
+        sc[g] = ok ? sc[g] : 0.f;
+        zz[g] = ok ? zz[g] : 0.f;
+      }
+      float s2[4];
+      {
+        float A[4] = {0.f, 0.f, 0.f, 0.f}, B[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t pe[4];
+#pragma unroll
+        for (int g2 = 0; g2 < NG; g2 += 2) {  // two groups per TMEM round trip (register budget)
+          uint32_t dq[2][8];
+          tmem_ld8(tmem + lane_base + T_DQK + 32 * g2 + 8 * k, dq[0]);
+          tmem_ld8(tmem + lane_base + T_DQK + 32 * (g2 + 1) + 8 * k, dq[1]);
+          if (g2 == 0) tmem_ld4(tmem + lane_base + T_DPE + 4 * k, pe);
+          tmem_wait_ld();
+          reg_fence(dq[0]);
+          reg_fence(dq[1]);
+          if (g2 == 0) reg_fence(pe);
+#pragma unroll
+          for (int gg = 0; gg < 2; ++gg) {
+            const int g = g2 + gg;
+            const float4 qs4 = *reinterpret_cast<const float4*>(F + F_QSUM + g * H + 4 * k);
+            const float qs[4] = {qs4.x, qs4.y, qs4.z, qs4.w};
+            const float scz = sc[g] * zz[g];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float qc = fmaf(__uint_as_float(dq[gg][4 + j]), 0.0625f, __uint_as_float(dq[gg][j]));
+              A[j] = fmaf(sc[g], qc, A[j]);
+              B[j] = fmaf(scz, qs[j], B[j]);
+            }
+          }
+        }
+        const float4 ki = *reinterpret_cast<const float4*>(F + F_KINV + 4 * k);
+        const float kinv[4] = {ki.x, ki.y, ki.z, ki.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          s2[j] = ok ? fmaf(A[j], kinv[j], __uint_as_float(pe[j]) - B[j]) * sl2 : -INFINITY;
+      }
+      // -- 1b. codes of tile i+1 into TMEM (QK^T(i) has completed) --
+      if (i + 1 < ntiles) {
+        const uint4 cws[2] = {cw0, cw1};
+#pragma unroll
+        for (int hv = 0; hv < 2; ++hv) {  // 16 columns at a time (register budget)
+          const uint32_t wd[4] = {cws[hv].x, cws[hv].y, cws[hv].z, cws[hv].w};
+          uint32_t r[16];
+#pragma unroll
+          for (int kq = 0; kq < 4; ++kq) {
+            r[4 * kq + 0] = wd[kq] & 0x03030303u;
+            r[4 * kq + 1] = wd[kq] & 0x0C0C0C0Cu;
+            r[4 * kq + 2] = (wd[kq] >> 4) & 0x03030303u;
+            r[4 * kq + 3] = (wd[kq] >> 4) & 0x0C0C0C0Cu;
+          }
+          tmem_st16(tmem + lane_base + T_AQK + 32 * k + 16 * hv, r);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&bars[B_AQK]);  // A of QK^T(i+1) is in TMEM, D of QK^T(i) has been read
+      } else {
+        tc_fence_before();
+      }
+      // -- 2. tile max per head (lane holds head 4k + 2*b4 + b3 after the exchange) and
+      //       per-quarter max of this thread's group scale --
+      {
+        const bool u16 = (lane & 16) != 0, u8 = (lane & 8) != 0;
+        const float b0 = fmaxf(u16 ? s2[2] : s2[0], __shfl_xor_sync(0xFFFFFFFFu, u16 ? s2[0] : s2[2], 16));
+        const float b1 = fmaxf(u16 ? s2[3] : s2[1], __shfl_xor_sync(0xFFFFFFFFu, u16 ? s2[1] : s2[3], 16));
+        float c = fmaxf(u8 ? b1 : b0, __shfl_xor_sync(0xFFFFFFFFu, u8 ? b0 : b1, 8));
+        c = fmaxf(c, __shfl_xor_sync(0xFFFFFFFFu, c, 4));
+        c = fmaxf(c, __shfl_xor_sync(0xFFFFFFFFu, c, 2));
+        c = fmaxf(c, __shfl_xor_sync(0xFFFFFFFFu, c, 1));
+        if ((lane & 7) == 0) F[F_HMAX + s * H * 4 + (4 * k + (lane >> 3)) * 4 + q4] = c;
+        float gm = sc[k];
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) gm = fmaxf(gm, __shfl_xor_sync(0xFFFFFFFFu, gm, o));
+        if (lane == 0) F[F_GMAX + s * NG * 4 + k * 4 + q4] = gm;
+      }
+      named_bar_sync(1, TOK_THREADS);
+      // -- 3. softmax against the reference max, P' = P s_g E_g as hi + lo / 16 (two E4M3
+      //       terms; the residual is scaled by 16 to stay in E4M3's normal range) --
+      float alpha[4], gf[NG], mt[4], gm[NG];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)  // all table reads first: one shared-memory round trip
+        mt[j] = max4(*reinterpret_cast<const float4*>(F + F_HMAX + s * H * 4 + (4 * k + j) * 4));
+#pragma unroll
+      for (int g = 0; g < NG; ++g) gm[g] = max4(*reinterpret_cast<const float4*>(F + F_GMAX + s * NG * 4 + g * 4));
+      bool resc = false;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const bool up = mt[j] > m_ref[j] + kTau;
+        alpha[j] = up ? ex2_approx(m_ref[j] - mt[j]) : 1.f;
+        m_ref[j] = up ? mt[j] : m_ref[j];
+        resc |= up;
+      }
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        const float en = group_e(gm[g]);
+        const bool up = i > 0 && gm[g] * E[g] >= kEMax;
+        gf[g] = up ? en / E[g] : 1.f;
+        E[g] = (i == 0 || up) ? en : E[g];
+        resc |= up;
+      }
+      if (resc) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          lsum[j] *= alpha[j];
+#pragma unroll
+          for (int g = 0; g < NG; ++g) y[g][j] *= alpha[j] * gf[g];
+        }
+        if (i > 0) {  // O holds PV(0..i-1): scale the columns of heads 4k.. (warp-uniform branch)
+          if (alive) alive = mbar_wait(&bars[B_PV], (i - 1) & 1, a.err);
+          __syncwarp();
+          tc_fence_after();
+#pragma unroll
+          for (int g = 0; g < NG; ++g) {
+            uint32_t v[8];
+            const uint32_t ta = tmem + lane_base + T_O + 32 * g + 8 * k;
+            tmem_ld8(ta, v);
+            tmem_wait_ld();
+            reg_fence(v);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) v[c] = __float_as_uint(__uint_as_float(v[c]) * (alpha[c & 3] * gf[g]));
+            tmem_st8(ta, v);
+          }
+          tmem_wait_st();
+          tc_fence_before();
+        }
+      }
+      float pj[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        pj[j] = ok ? ex2_approx(s2[j] - m_ref[j]) : 0.f;
+        lsum[j] += pj[j];
+      }
+      uint8_t* pb = smem + OFF_PB + s * PB_BUF;
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        const float se = sc[g] * E[g];
+        uint32_t hw = 0, lw = 0;
+#pragma unroll
+        for (int jp = 0; jp < 2; ++jp) {
+          const __half2 hx = __floats2half2_rn(pj[2 * jp] * se, pj[2 * jp + 1] * se);
+          const uint32_t hq = half2_to_e4m3x2(hx);
+          const __half2 hf = e4m3x2_to_half2(hq);
+          const uint32_t lq = half2_to_e4m3x2(__hmul2(__hsub2(hx, hf), __float2half2_rn(16.f)));
+          const float2 v = __half22float2(__hfma2(e4m3x2_to_half2(lq), __float2half2_rn(0.0625f), hf));
+          y[g][2 * jp] = fmaf(v.x, zz[g], y[g][2 * jp]);
+          y[g][2 * jp + 1] = fmaf(v.y, zz[g], y[g][2 * jp + 1]);
+          hw |= hq << (16 * jp);
+          lw |= lq << (16 * jp);
+        }
+        *reinterpret_cast<uint2*>(pb + g * PB_GROUP + sw32(t, 8 * k)) = make_uint2(hw, lw);
+      }
+      fence_proxy_async();
+      // -- 4. the PV-A tile of i+1 into buffer (i+1) & 1, last read by PV(i-1) --
+      if (i + 1 < ntiles) {
+        if (alive && i >= 1) alive = mbar_wait(&bars[B_PV], (i - 1) & 1, a.err);
+        uint32_t r[32];
+        expand(r);
+        store_pva((i + 1) & 1, r);
+        ok = ok_next;
+        if (i + 2 < ntiles) {
+          load_tile(i + 2, pg_ahead);
+          pg_ahead = page_raw(i + 3, t >> 6);
+        }
+      }
+      fence_proxy_async();
+      mbar_arrive(&bars[B_PREADY]);  // P'(i), the PV-A tile of i+1 and a rescaled O are ready;
+                                     // params stage i & 1 has been read
+    }
+    // -- final: sum P and sum P' z over the warp's 32 tokens --
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float l = lsum[j];
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
+      if (lane == 0) F[F_FINL + q4 * H + 4 * k + j] = l;
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        float yy = y[g][j];
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) yy += __shfl_xor_sync(0xFFFFFFFFu, yy, o);
+        if (lane == 0) F[F_FINY + (q4 * NG + g) * H + 4 * k + j] = yy;
+      }
+    }
+    named_bar_sync(3, TOK_THREADS);
+    float lt[4];  // sum P over the split per head 4k + j
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      lt[j] = 0.f;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) lt[j] += F[F_FINL + w * H + 4 * k + j];
+    }
+    if (q4 == 0 && lane == 0) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        a.part_lse[(static_cast<int64_t>(b) * H + 4 * k + j) * S + split] =
+            lt[j] > 0.f ? (m_ref[j] + __log2f(lt[j])) * kLn2 : -INFINITY;
+    }
+    // -- O rows of this lane quarter (M row = permuted element), columns of heads 4k.. --
+    if (alive) alive = mbar_wait(&bars[B_PV], (ntiles - 1) & 1, a.err);
+    __syncwarp();
+    tc_fence_after();
+    const float rs = ((t >> 2) & 1) ? 128.f : 512.f;  // 2^9 / (1 or 4): the element's code weight
+    float* po = a.part_o + (static_cast<int64_t>(b) * H * S + split) * D + kperm(t);
+    const int hs = S * D;  // head stride of part_o
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      uint32_t v[8];
+      tmem_ld8(tmem + lane_base + T_O + 32 * g + 8 * k, v);
+      tmem_wait_ld();
+      reg_fence(v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float yy = 0.f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) yy += F[F_FINY + (w * NG + g) * H + 4 * k + j];
+        const float dh = fmaf(__uint_as_float(v[4 + j]), 0.0625f, __uint_as_float(v[j]));
+        po[(4 * k + j) * hs + 128 * g] = lt[j] > 0.f ? (dh * rs - yy) / (E[g] * lt[j]) : 0.f;
+      }
+    }
+    tc_fence_before();
+  } else if (lane == 0) {
+    // ---- issuer: k_pe TMA, L2 prefetch, QK^T and PV issue --------------------------------------
+    prefetch_tensormap(&tm_rope);
+    // page ids of tiles i+1 .. i+5, fetched five tiles ahead
+    int32_t r1a = page_raw(1, 0), r1b = page_raw(1, 1), r2a = page_raw(2, 0), r2b = page_raw(2, 1);
+    int32_t r3a = page_raw(3, 0), r3b = page_raw(3, 1), r4a = page_raw(4, 0), r4b = page_raw(4, 1);
+    int32_t r5a = page_raw(5, 0), r5b = page_raw(5, 1);
+    {
+      const int32_t r0a = page_raw(0, 0), r0b = page_raw(0, 1);
+      issue_kpe(0, r0a, r0b);
+      issue_params(0, r0a, r0b);
+    }
+    if (ntiles > 1) {
+      issue_kpe(1, r1a, r1b);
+      issue_params(1, r1a, r1b);
+    }
+    if (ntiles > 2) prefetch_tile(2, r2a, r2b);
+    if (ntiles > 3) prefetch_tile(3, r3a, r3b);
+    for (int i = 0; i < ntiles; ++i) {
+      if (alive) alive = mbar_wait(&bars[B_AQK], i & 1, a.err);
+      if (alive) alive = mbar_wait(&bars[B_KPE + (i & 1)], (i >> 1) & 1, a.err);
+      tc_fence_after();
+      issue_qk(i);
+      if (i >= 1) {
+        if (alive) alive = mbar_wait(&bars[B_PREADY], (i - 1) & 1, a.err);
+        tc_fence_after();
+        issue_pv(i - 1);
+        if (i + 1 < ntiles) issue_params(i + 1, r1a, r1b);  // stage (i+1) & 1 held tile i-1, read before P'(i-1)
+      }
+      if (i + 2 < ntiles) {  // stage i & 1 is free once QK^T(i) has completed
+        if (alive) alive = mbar_wait(&bars[B_QK], i & 1, a.err);
+        issue_kpe(i + 2, r2a, r2b);
+      }
+      if (i + 4 < ntiles) prefetch_tile(i + 4, r4a, r4b);
+      r1a = r2a, r1b = r2b, r2a = r3a, r2b = r3b, r3a = r4a, r3b = r4b, r4a = r5a, r4b = r5b;
+      r5a = page_raw(i + 6, 0);
+      r5b = page_raw(i + 6, 1);
+    }
+    if (alive) alive = mbar_wait(&bars[B_PREADY], (ntiles - 1) & 1, a.err);
+    tc_fence_after();
+    issue_pv(ntiles - 1);
+  }
+
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace tc
+
+static int map_rope(CUtensorMap* map, const void* base, uint64_t rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return ROLAQ_ECUDA;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(tc::DR), rows};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(tc::DR * 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(tc::DR), static_cast<cuuint32_t>(tc::PAGE)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? ROLAQ_OK : ROLAQ_ECUDA;
+}
+
+bool decode_tc_supported(const DecodeArgs& a, int heads) {
+  return a.cache.latent_dim == tc::D && a.cache.rope_dim == tc::DR && heads == tc::H && (a.q_sh % 8) == 0 &&
+         (a.q_sb % 8) == 0 && (reinterpret_cast<uintptr_t>(a.q) & 15) == 0;
+}
+
+int launch_decode_tc(const DecodeArgs& a, cudaStream_t s) {
+  CUtensorMap mr;
+  int rc = map_rope(&mr, a.cache.rope, static_cast<uint64_t>(a.cache.num_slots));
+  if (rc != ROLAQ_OK) return rc;
+  static const bool attr_ok = cudaFuncSetAttribute(tc::decode_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   (int)tc::SMEM) == cudaSuccess;
+  if (!attr_ok) return ROLAQ_ECUDA;
+  dim3 grid(a.num_splits, a.batch);
+  tc::decode_tc_kernel<<<grid, tc::THREADS, tc::SMEM, s>>>(mr, a);
+  return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;
+}
+
+}  // namespace rolaq

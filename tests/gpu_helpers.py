@@ -49,9 +49,11 @@ class GpuPool:
 
 
 def fill_requests(pool: GpuPool, seq_lens, page_table: torch.Tensor, rotation: torch.Tensor, codec, seed=0,
-                  positions_mode=True):
+                  positions_mode=True, row_gain=None):
     """Prefill every request with seeded latents through the fused writer.
 
+    ``row_gain(L) -> [L]`` (optional) multiplies each token's latent and rope rows, e.g.
+    to make group scales and scores drift along the sequence.
     Returns the BF16 inputs (c_kv, k_pe) per request for oracle checks.
     """
     dev = pool.codes.device
@@ -64,6 +66,10 @@ def fill_requests(pool: GpuPool, seq_lens, page_table: torch.Tensor, rotation: t
             continue
         c_kv = synth.latents(L, pool.d, seed + 17 * b, dev, scale=scale)
         k_pe = synth.normal_bf16((L, pool.dr), seed + 31 * b + 5, dev)
+        if row_gain is not None:
+            gain = row_gain(L).to(dev).float()[:, None]
+            c_kv = (c_kv.float() * gain).to(torch.bfloat16)
+            k_pe = (k_pe.float() * gain).to(torch.bfloat16)
         pos = torch.arange(L, device=dev)
         slots = (page_table[b, pos // 64].long() * 64 + pos % 64).contiguous()
         seq = torch.full((L,), L, dtype=torch.int32, device=dev)

@@ -19,7 +19,7 @@ pytestmark = pytest.mark.gpu
 SHAPES = [(512, 64, 16), (256, 32, 40), (512, 64, 8), (256, 32, 16)]
 
 
-def _setup(d, dr, seq_lens, max_pages=None, seed=0, sink=4, recent=16):
+def _setup(d, dr, seq_lens, max_pages=None, seed=0, sink=4, recent=16, row_gain=None):
     b = len(seq_lens)
     mp = max_pages or max(1, max((L + 63) // 64 for L in seq_lens))
     g = torch.Generator().manual_seed(seed)
@@ -29,7 +29,7 @@ def _setup(d, dr, seq_lens, max_pages=None, seed=0, sink=4, recent=16):
     pool = GpuPool(64 * (total + 1), d, dr, max_reqs=b, sink=sink, recent=recent)
     r = synth.rotation(d, seed=seed + 5)
     codec = ops.codec_serving(0.85, synth.signal_gain(0.85))
-    fill_requests(pool, seq_lens, pt, r, codec, seed=seed)
+    fill_requests(pool, seq_lens, pt, r, codec, seed=seed, row_gain=row_gain)
     return pool, pt
 
 
@@ -80,6 +80,38 @@ def test_decode_matches_oracle(d, dr, h, splits):
     ref, ref_lse = odecode.decode(pool.to_oracle(), bits(q), pt.cpu().numpy(), seq_lens, sm)
     _check(out, ref, seq_lens, fp32_result(part_o, part_lse))
     assert np.allclose(lse.cpu().numpy(), ref_lse, atol=2e-3)
+
+
+@pytest.mark.parametrize("direction", ["rising", "falling"])
+def test_decode_drifting_scales_and_scores(direction):
+    """Group scales and scores that drift 2^6 along the sequence: the kernel's running
+    reference max and per-group weight scale both move many times inside a split."""
+    d, dr, h = 512, 64, 16
+    seq_lens = [3000, 2200]
+
+    def gain(L):
+        x = torch.arange(L, dtype=torch.float64) / L
+        return torch.exp2(6.0 * (x if direction == "rising" else 1.0 - x))
+
+    pool, pt = _setup(d, dr, seq_lens, seed=21, row_gain=gain)
+    b = len(seq_lens)
+    q = synth.normal_bf16((b, h, d + dr), seed=4, device="cuda")
+    sl = torch.tensor(seq_lens, dtype=torch.int32, device="cuda")
+    splits = 2
+    part_o = torch.empty(b, h, splits + 1, d, device="cuda")
+    part_lse = torch.empty(b, h, splits + 1, device="cuda")
+    out = torch.empty(b, h, d, dtype=torch.bfloat16, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    sm = 0.02  # keeps the softmax from collapsing onto a single token at the largest gain
+    ops.packed_decode(q, pool.view(), pt, sl, sm, splits, part_o, part_lse, out, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref, _ = odecode.decode(pool.to_oracle(), bits(q), pt.cpu().numpy(), seq_lens, sm)
+    o32 = fp32_result(part_o, part_lse)
+    for i in range(b):
+        scale = max(1.0, float(np.abs(ref[i]).max()))
+        assert np.abs(o32[i] - ref[i]).max() <= 2e-2 * scale
+        assert cosine(o32[i], ref[i]) >= 0.9995
 
 
 def test_decode_zero_length_and_window_only():
@@ -144,8 +176,16 @@ def test_decode_token_range_partials_merge_to_full():
     merged = torch.empty(b * h, d, device="cuda")
     ops.merge_partials(torch.stack(outs), torch.stack(lses), out_f32=merged)
     torch.cuda.synchronize()
-    diff = np.abs(merged.view(b, h, d).cpu().numpy() - full32).max()
-    assert diff <= 1e-3
+    # Slicing the sequence moves the tile boundaries that the attention weights are
+    # quantised against (two E4M3 terms: ~2^-9 relative per weight, the precision of
+    # the BF16 weights in the reference's P.V), so the two FP32 results agree to the
+    # weight precision, not bit for bit; both are checked against the oracle as well.
+    merged_np = merged.view(b, h, d).cpu().numpy()
+    diff = np.abs(merged_np - full32).max()
+    assert diff <= 4e-3
+    ref, _ = odecode.decode(pool.to_oracle(), bits(q), pt.cpu().numpy(), seq_lens, 0.07)
+    for i in range(b):
+        assert np.abs(merged_np[i] - ref[i]).max() <= 2e-2
 
 
 def test_decode_bad_page_is_reported():
