@@ -195,11 +195,7 @@ __global__ void __launch_bounds__(kWinHeads * 32) window_rows_kernel(const Decod
   const int s2 = min(max(rs, hs), L), e2 = max(min(re, L), s2);
   const int n1 = e1 - s1;
   const int nw = n1 + (e2 - s2);  // <= sink + recent <= kMaxWindow (checked by the host)
-  for (int idx = tid; idx < kWinHeads * KW; idx += blockDim.x) {
-    const int h = idx / KW, e = idx % KW;
-    qf[idx] = bf16f(a.q[b * a.q_sb + (h0 + h) * a.q_sh + e]);
-  }
-  if (tid < nw) {  // per row: slot and the ring row that holds it (if any)
+  if (tid < nw) {  // per row: slot and the ring row that holds it (if any); first, as the longest chain
     const int pos = tid < n1 ? s1 + tid : s2 + (tid - n1);
     const int64_t page = a.page_table[b * a.pt_stride + pos / kPage];
     int64_t slot = -1, r = -1;
@@ -213,8 +209,20 @@ __global__ void __launch_bounds__(kWinHeads * 32) window_rows_kernel(const Decod
     rslot[tid] = slot;
     rrow[tid] = r;
   }
+  // queries of the 4 heads as FP32, 8 BF16 per 16-byte load (rows 16-byte aligned on this path)
+  for (int idx = tid; idx < kWinHeads * (KW / 8); idx += blockDim.x) {
+    const int h = idx / (KW / 8), c = idx % (KW / 8);
+    const uint4 w = *reinterpret_cast<const uint4*>(a.q + b * a.q_sb + (h0 + h) * a.q_sh + 8 * c);
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      qf[h * KW + 8 * c + 2 * u] = __uint_as_float(ws[u] << 16);
+      qf[h * KW + 8 * c + 2 * u + 1] = __uint_as_float(ws[u] & 0xFFFF0000u);
+    }
+  }
   __syncthreads();
-  for (int p = warp; p < nw; p += kWinHeads) {
+  static_assert(D % 256 == 0 && DR % 8 == 0 && DR / 8 <= 32, "window row gather shape");
+  for (int p = warp; p < nw; p += kWinHeads) {  // warp per row, 16-byte loads
     const int64_t slot = rslot[p], r = rrow[p];
     float* dst = kw + p * KP;
     if (slot < 0) {
@@ -222,15 +230,35 @@ __global__ void __launch_bounds__(kWinHeads * 32) window_rows_kernel(const Decod
       continue;
     }
     if (r >= 0) {
-      for (int e = lane; e < D; e += 32) dst[e] = bf16f(a.cache.hp[r * D + e]);
+#pragma unroll
+      for (int u = 0; u < D / 256; ++u) {
+        const int e0 = 8 * lane + 256 * u;
+        const uint4 w = *reinterpret_cast<const uint4*>(a.cache.hp + r * D + e0);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          dst[e0 + 2 * v] = __uint_as_float(ws[v] << 16);
+          dst[e0 + 2 * v + 1] = __uint_as_float(ws[v] & 0xFFFF0000u);
+        }
+      }
     } else {
-      for (int e = lane; e < D; e += 32) {
-        const uint32_t c = (a.cache.codes[slot * (D / 4) + e / 4] >> (2 * (e % 4))) & 3u;
-        const float2 sz = reinterpret_cast<const float2*>(a.cache.params)[slot * (D / 128) + e / 128];
-        dst[e] = __fmul_rn(__fsub_rn(static_cast<float>(c), sz.y), sz.x);
+      for (int e0 = 16 * lane; e0 < D; e0 += 16 * 32) {  // 16 codes (one 32-bit word) per step
+        const uint32_t cw = *reinterpret_cast<const uint32_t*>(a.cache.codes + slot * (D / 4) + e0 / 4);
+        const float2 sz = reinterpret_cast<const float2*>(a.cache.params)[slot * (D / 128) + e0 / 128];
+#pragma unroll
+        for (int v = 0; v < 16; ++v)
+          dst[e0 + v] = __fmul_rn(__fsub_rn(static_cast<float>((cw >> (2 * v)) & 3u), sz.y), sz.x);
       }
     }
-    for (int e = lane; e < DR; e += 32) dst[D + e] = bf16f(a.cache.rope[slot * DR + e]);
+    if (lane < DR / 8) {
+      const uint4 w = *reinterpret_cast<const uint4*>(a.cache.rope + slot * DR + 8 * lane);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        dst[D + 8 * lane + 2 * v] = __uint_as_float(ws[v] << 16);
+        dst[D + 8 * lane + 2 * v + 1] = __uint_as_float(ws[v] & 0xFFFF0000u);
+      }
+    }
   }
   __syncthreads();
   {  // warp = head, lane = row
