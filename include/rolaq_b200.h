@@ -189,6 +189,24 @@ int rolaq_packed_decode(const uint16_t* q, int64_t q_stride_b, int64_t q_stride_
                         int32_t* err, cudaStream_t stream);
 
 /*
+ * rolaq_packed_decode with the split partials (part_o, part_lse) in a fixed 32 MiB
+ * device array of this library instead of caller scratch: for callers that cannot
+ * allocate at decode time.  No counterpart in the reference (its decode always takes
+ * attn_logits / attn_lse from the caller).  Limit: batch * heads * (num_splits + 1) *
+ * (latent_dim + 1) <= rolaq_packed_decode_static_capacity() floats, else ROLAQ_EINVAL.
+ * The first call on a device resolves the array's address (cudaGetSymbolAddress) and
+ * should come before any stream capture; nothing in the array needs to start at zero;
+ * calls that overlap in time on one device share the array and race.
+ */
+int64_t rolaq_packed_decode_static_capacity(void);
+int rolaq_packed_decode_static(const uint16_t* q, int64_t q_stride_b, int64_t q_stride_h, int32_t batch,
+                               int32_t heads, const rolaq_layer_cache* cache, const int32_t* page_table,
+                               int64_t pt_stride, int32_t max_pages, const int32_t* seq_lens,
+                               const int32_t* token_range, float sm_scale, int32_t num_splits,
+                               uint16_t* out, int64_t out_stride_b, int64_t out_stride_h, float* out_lse,
+                               int32_t* err, cudaStream_t stream);
+
+/*
  * LSE merge of normalised partials: for each row r in [0, rows) and part p in
  * [0, n_parts): o = part_o + r*row_stride + p*part_stride (D floats),
  * lse = part_lse[r*lse_row_stride + p*lse_part_stride] (natural log, -inf = empty).

@@ -36,6 +36,8 @@ EXPORTS = (
     "rolaq_dequant_rows",
     "rolaq_prepare_gf_splits",
     "rolaq_packed_decode",
+    "rolaq_packed_decode_static_capacity",
+    "rolaq_packed_decode_static",
     "rolaq_merge_partials",
 )
 
@@ -97,6 +99,11 @@ _SIGS = {
     "rolaq_packed_decode": (
         INT,
         [P, I64, I64, I32, I32, ctypes.POINTER(LayerCache), P, I64, I32, P, P, F32, I32, P, P, P, I64, I64, P, P, P],
+    ),
+    "rolaq_packed_decode_static_capacity": (I64, []),
+    "rolaq_packed_decode_static": (
+        INT,
+        [P, I64, I64, I32, I32, ctypes.POINTER(LayerCache), P, I64, I32, P, P, F32, I32, P, I64, I64, P, P, P],
     ),
     "rolaq_merge_partials": (INT, [P, I64, I64, P, I64, I64, I32, I64, I32, P, P, I64, P, P]),
 }

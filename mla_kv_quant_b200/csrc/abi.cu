@@ -285,3 +285,68 @@ int rolaq_merge_partials(const float* part_o, int64_t row_stride, int64_t part_s
 }
 
 }  // extern "C"
+
+// ---- rolaq_packed_decode_static: the split partials in a fixed device array --------------------
+// For callers that cannot allocate at decode time.  The scratch (part_o followed by part_lse,
+// 32 MiB of FP32) is a file-scope device array of this library; its address is resolved once
+// per device (the first call on a device, which should come before any stream capture) and
+// cached.  Every element a call reads is written earlier in the same call, so nothing needs to
+// start at zero; two calls that overlap in time on one device (any streams) share the array
+// and race.
+namespace {
+
+constexpr int64_t kStaticPartFloats = int64_t(8) << 20;
+__device__ __align__(256) float g_static_parts[kStaticPartFloats];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+float* g_static_ptr[kMaxDevices] = {};
+
+int static_parts(float** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(ROLAQ_ECUDA, "no CUDA device");
+  if (dev < 0 || dev >= kMaxDevices) return fail(ROLAQ_EUNSUPPORTED, "device ordinal %d >= %d", dev, kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (g_static_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_parts);
+    if (e != cudaSuccess) return fail(ROLAQ_ECUDA, "cudaGetSymbolAddress(static decode scratch): %s", cudaGetErrorString(e));
+    g_static_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_static_ptr[dev];
+  return ROLAQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t rolaq_packed_decode_static_capacity(void) { return kStaticPartFloats; }
+
+int rolaq_packed_decode_static(const uint16_t* q, int64_t q_stride_b, int64_t q_stride_h, int32_t batch,
+                               int32_t heads, const rolaq_layer_cache* cache, const int32_t* page_table,
+                               int64_t pt_stride, int32_t max_pages, const int32_t* seq_lens,
+                               const int32_t* token_range, float sm_scale, int32_t num_splits, uint16_t* out,
+                               int64_t out_stride_b, int64_t out_stride_h, float* out_lse, int32_t* err,
+                               cudaStream_t stream) {
+  if (batch < 0 || heads <= 0 || num_splits < 1 || num_splits > 1024 || batch > 65535 || heads > 1024)
+    return fail(ROLAQ_EINVAL, "batch, heads or num_splits out of range");
+  if (cache == nullptr) return fail(ROLAQ_EINVAL, "cache is NULL");
+  const int64_t d = cache->latent_dim;
+  if (d <= 0 || d > 4096) return fail(ROLAQ_EINVAL, "latent_dim out of range");
+  const int64_t rows = int64_t(batch) * heads * (num_splits + 1);
+  const int64_t need = rows * d + rows;  // part_o [B, H, S+1, D] then part_lse [B, H, S+1]
+  if (need > kStaticPartFloats)
+    return fail(ROLAQ_EINVAL,
+                "static decode scratch holds %lld floats; batch %d x heads %d x (num_splits + 1) %d x "
+                "(latent_dim + 1) needs %lld (use rolaq_packed_decode with caller scratch)",
+                (long long)kStaticPartFloats, batch, heads, num_splits + 1, (long long)need);
+  if (batch == 0) return ROLAQ_OK;
+  float* base = nullptr;
+  if (int rc = static_parts(&base)) return rc;
+  return rolaq_packed_decode(q, q_stride_b, q_stride_h, batch, heads, cache, page_table, pt_stride, max_pages,
+                             seq_lens, token_range, sm_scale, num_splits, base, base + rows * d, out, out_stride_b,
+                             out_stride_h, out_lse, err, stream);
+}
+
+}  // extern "C"

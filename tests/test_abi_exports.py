@@ -17,7 +17,7 @@ HEADER = Path(__file__).resolve().parents[1] / "include" / "rolaq_b200.h"
 
 def declared():
     text = HEADER.read_text()
-    return sorted(set(re.findall(r"^(?:int|const char\*)\s+(rolaq_\w+)\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^(?:int|int64_t|const char\*)\s+(rolaq_\w+)\(", text, flags=re.M)))
 
 
 def test_header_lists_every_binding():
