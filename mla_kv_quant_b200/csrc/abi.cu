@@ -249,6 +249,10 @@ int rolaq_packed_decode(const uint16_t* q, int64_t q_stride_b, int64_t q_stride_
   a.part_o = part_o;
   a.part_lse = part_lse;
   a.err = err;
+  {
+    const int fused = launch_decode_merged(a, heads, out, out_stride_b, out_stride_h, out_lse, stream);
+    if (fused != ROLAQ_EUNSUPPORTED) return cuda_rc(fused, "packed_decode");
+  }
   int rc = cuda_rc(launch_decode(a, heads, stream), "packed_decode");
   if (rc != ROLAQ_OK) return rc;
   const int parts = num_splits + 1;

@@ -729,33 +729,253 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
 
 // ---- LSE merge of normalised partials -----------------------------------------------------
 
+// One CTA per row.  The part weights exp(lse_p - m) / sum are computed once into shared
+// memory; with VEC each thread then reads 4 consecutive elements of every part with 16-byte
+// loads (all parts in flight at once) and writes 4 outputs (8-byte BF16 stores).
+template <bool VEC>
 __global__ void merge_kernel(const float* __restrict__ part_o, int64_t row_stride, int64_t part_stride,
                              const float* __restrict__ part_lse, int64_t lse_row_stride, int64_t lse_part_stride,
                              int n_parts, int d, uint16_t* __restrict__ out_bf16, float* __restrict__ out_f32,
                              int64_t ld_out, float* __restrict__ out_lse) {
+  extern __shared__ float wts[];  // [n_parts]
+  __shared__ float red[2];
   const int64_t row = blockIdx.x;
   const float* lse = part_lse + row * lse_row_stride;
-  float m = -INFINITY;
-  for (int p = 0; p < n_parts; ++p) m = fmaxf(m, lse[p * lse_part_stride]);
-  const float mref = m == -INFINITY ? 0.f : m;
-  float den = 0.f;
-  for (int p = 0; p < n_parts; ++p) den += __expf(lse[p * lse_part_stride] - mref);
+  if (threadIdx.x < 32) {
+    float m = -INFINITY;
+    for (int p = threadIdx.x; p < n_parts; p += 32) m = fmaxf(m, lse[p * lse_part_stride]);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    const float mref = m == -INFINITY ? 0.f : m;
+    float den = 0.f;
+    for (int p = threadIdx.x; p < n_parts; p += 32) {
+      const float w = __expf(lse[p * lse_part_stride] - mref);
+      wts[p] = w;
+      den += w;
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) den += __shfl_xor_sync(0xFFFFFFFFu, den, o);
+    if (threadIdx.x == 0) {
+      red[0] = mref;
+      red[1] = den;
+    }
+  }
+  __syncthreads();
+  const float mref = red[0], den = red[1];
   const float inv = den > 0.f ? 1.f / den : 0.f;
   const float* po = part_o + row * row_stride;
-  for (int j = threadIdx.x; j < d; j += blockDim.x) {
-    float acc = 0.f;
-    for (int p = 0; p < n_parts; ++p) {
-      const float w = __expf(lse[p * lse_part_stride] - mref);
-      if (w > 0.f) acc = fmaf(w, po[p * part_stride + j], acc);
+  if (VEC) {
+    for (int j = 4 * threadIdx.x; j < d; j += 4 * blockDim.x) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+      for (int p = 0; p < n_parts; ++p) {  // unconditional loads (all in flight); empty parts masked
+        const float w = wts[p];
+        const float4 v = *reinterpret_cast<const float4*>(po + p * part_stride + j);
+        acc.x = w > 0.f ? fmaf(w, v.x, acc.x) : acc.x;
+        acc.y = w > 0.f ? fmaf(w, v.y, acc.y) : acc.y;
+        acc.z = w > 0.f ? fmaf(w, v.z, acc.z) : acc.z;
+        acc.w = w > 0.f ? fmaf(w, v.w, acc.w) : acc.w;
+      }
+      acc.x *= inv;
+      acc.y *= inv;
+      acc.z *= inv;
+      acc.w *= inv;
+      if (out_f32) *reinterpret_cast<float4*>(out_f32 + row * ld_out + j) = acc;
+      if (out_bf16) {
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+        *reinterpret_cast<uint2*>(out_bf16 + row * ld_out + j) =
+            make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+      }
     }
-    acc *= inv;
-    if (out_f32) out_f32[row * ld_out + j] = acc;
-    if (out_bf16) {
-      const __nv_bfloat16 h = __float2bfloat16_rn(acc);
-      out_bf16[row * ld_out + j] = *reinterpret_cast<const uint16_t*>(&h);
+  } else {
+    for (int j = threadIdx.x; j < d; j += blockDim.x) {
+      float acc = 0.f;
+      for (int p = 0; p < n_parts; ++p) {
+        const float w = wts[p];
+        if (w > 0.f) acc = fmaf(w, po[p * part_stride + j], acc);
+      }
+      acc *= inv;
+      if (out_f32) out_f32[row * ld_out + j] = acc;
+      if (out_bf16) {
+        const __nv_bfloat16 h = __float2bfloat16_rn(acc);
+        out_bf16[row * ld_out + j] = *reinterpret_cast<const uint16_t*>(&h);
+      }
     }
   }
   if (threadIdx.x == 0 && out_lse) out_lse[row] = den > 0.f ? mref + logf(den) : -INFINITY;
+}
+
+// Window split + LSE merge for the tcgen05 path, one CTA per (request, head): the window
+// rows are gathered once per CTA (lookups by one thread per row, 16-byte loads by a warp per
+// row), scored against this head's query (a warp per row, lanes over the 576 elements, a
+// shuffle sum), softmaxed, and their partial is merged with the num_splits INT2 partials the
+// tcgen05 kernel wrote.  The window partial is also stored in split num_splits of
+// part_o / part_lse, so the scratch holds every partial after the call as before.
+template <int D, int DR>
+__global__ void __launch_bounds__(128) merge_window_kernel(const DecodeArgs a, int heads, uint16_t* __restrict__ out,
+                                                           int64_t out_sb, int64_t out_sh, float* __restrict__ out_lse,
+                                                           int nw_cap) {
+  constexpr int KW = D + DR, KP = KW + 1;
+  static_assert(D == 4 * 128, "four outputs per thread");
+  extern __shared__ float dyn[];
+  float* kw = dyn;                 // [nw_cap][KP]
+  float* wts = kw + nw_cap * KP;   // [num_splits]
+  __shared__ float sc[kMaxWindow];
+  __shared__ int64_t rslot[kMaxWindow], rrow[kMaxWindow];
+  __shared__ float stat[4];
+  const int row = blockIdx.x, b = row / heads, h = row % heads;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int S = a.num_splits + 1;
+  int L = a.seq_lens[b];
+  if (L < 0) L = 0;
+  if (L > a.max_pages * kPage) L = a.max_pages * kPage;
+  const int P = a.cache.sink, W = a.cache.recent;
+  const int lo = min(P, L);
+  const int hs = max(lo, L - W);
+  int rs = 0, re = L;
+  if (a.token_range != nullptr) {
+    rs = max(0, a.token_range[2 * b]);
+    re = min(L, a.token_range[2 * b + 1]);
+  }
+  const int s1 = min(max(rs, 0), lo), e1 = max(min(re, lo), s1);
+  const int s2 = min(max(rs, hs), L), e2 = max(min(re, L), s2);
+  const int n1 = e1 - s1;
+  const int nw = n1 + (e2 - s2);  // <= sink + recent = nw_cap
+  if (tid < nw) {
+    const int pos = tid < n1 ? s1 + tid : s2 + (tid - n1);
+    const int64_t page = a.page_table[b * a.pt_stride + pos / kPage];
+    int64_t slot = -1, r = -1;
+    if (page >= 0 && (page + 1) * kPage <= a.cache.num_slots) {
+      slot = page * kPage + pos % kPage;
+      r = a.cache.rows ? a.cache.rows[slot] : -1;
+      if (!(r >= 0 && r < a.cache.num_ring_rows && a.cache.owners[r] == slot)) r = -1;
+    } else {
+      report(a.err, ROLAQ_DEV_BAD_PAGE);
+    }
+    rslot[tid] = slot;
+    rrow[tid] = r;
+  }
+  // this head's query, 18 elements per lane (e = lane + 32 u)
+  constexpr int QE = KW / 32;
+  static_assert(KW % 32 == 0, "query slice per lane");
+  float qv[QE];
+  {
+    const uint16_t* qh = a.q + b * a.q_sb + h * a.q_sh;
+#pragma unroll
+    for (int u = 0; u < QE; ++u) qv[u] = bf16f(qh[lane + 32 * u]);
+  }
+  __syncthreads();
+  for (int p = warp; p < nw; p += 4) {
+    const int64_t slot = rslot[p], r = rrow[p];
+    float* dst = kw + p * KP;
+    if (slot < 0) {
+      for (int e = lane; e < KW; e += 32) dst[e] = 0.f;
+    } else {
+      if (r >= 0) {
+#pragma unroll
+        for (int u = 0; u < D / 256; ++u) {
+          const int e0 = 8 * lane + 256 * u;
+          const uint4 w = *reinterpret_cast<const uint4*>(a.cache.hp + r * D + e0);
+          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            dst[e0 + 2 * v] = __uint_as_float(ws[v] << 16);
+            dst[e0 + 2 * v + 1] = __uint_as_float(ws[v] & 0xFFFF0000u);
+          }
+        }
+      } else {
+        for (int e0 = 16 * lane; e0 < D; e0 += 16 * 32) {
+          const uint32_t cw = *reinterpret_cast<const uint32_t*>(a.cache.codes + slot * (D / 4) + e0 / 4);
+          const float2 sz = reinterpret_cast<const float2*>(a.cache.params)[slot * (D / 128) + e0 / 128];
+#pragma unroll
+          for (int v = 0; v < 16; ++v)
+            dst[e0 + v] = __fmul_rn(__fsub_rn(static_cast<float>((cw >> (2 * v)) & 3u), sz.y), sz.x);
+        }
+      }
+      if (lane < DR / 8) {
+        const uint4 w = *reinterpret_cast<const uint4*>(a.cache.rope + slot * DR + 8 * lane);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          dst[D + 8 * lane + 2 * v] = __uint_as_float(ws[v] << 16);
+          dst[D + 8 * lane + 2 * v + 1] = __uint_as_float(ws[v] & 0xFFFF0000u);
+        }
+      }
+    }
+    __syncwarp();
+    float acc = 0.f;
+#pragma unroll
+    for (int u = 0; u < QE; ++u) acc = fmaf(qv[u], dst[lane + 32 * u], acc);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+    if (lane == 0) sc[p] = acc * a.sm_scale;
+  }
+  // INT2 part weights need only the LSEs: warp 1 prepares them while warp 0 does the window softmax
+  __syncthreads();
+  const float* lse_row = a.part_lse + static_cast<int64_t>(row) * S;
+  if (warp == 0) {
+    const float x = lane < nw ? sc[lane] : -INFINITY;
+    float m = x;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    const float e = lane < nw ? __expf(x - m) : 0.f;
+    float l = e;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
+    if (lane < nw) sc[lane] = e;
+    if (lane == 0) {
+      stat[0] = nw > 0 ? m + logf(l) : -INFINITY;  // window lse
+      stat[1] = l;
+    }
+  } else if (warp == 1) {
+    float m = -INFINITY;
+    for (int p = lane; p < a.num_splits; p += 32) m = fmaxf(m, lse_row[p]);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    if (lane == 0) stat[2] = m;
+  }
+  __syncthreads();
+  const float lse_w = stat[0], lw = stat[1];
+  const float mref0 = fmaxf(stat[2], lse_w);
+  const float mref = mref0 == -INFINITY ? 0.f : mref0;
+  float den = 0.f;  // every thread sums the same weights in the same order
+  for (int p = tid; p < a.num_splits; p += blockDim.x) wts[p] = __expf(lse_row[p] - mref);
+  __syncthreads();
+  for (int p = 0; p < a.num_splits; ++p) den += wts[p];
+  const float ww = lse_w == -INFINITY ? 0.f : __expf(lse_w - mref);
+  den += ww;
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  // window partial (this thread's 4 elements), stored as split num_splits, then the merge
+  const int j = 4 * tid;
+  float4 ow = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int p = 0; p < nw; ++p) {
+    const float e = sc[p];
+    const float* k = kw + p * KP + j;
+    ow.x = fmaf(e, k[0], ow.x);
+    ow.y = fmaf(e, k[1], ow.y);
+    ow.z = fmaf(e, k[2], ow.z);
+    ow.w = fmaf(e, k[3], ow.w);
+  }
+  const float il = nw > 0 ? 1.f / lw : 0.f;
+  ow = make_float4(ow.x * il, ow.y * il, ow.z * il, ow.w * il);
+  float* prow = a.part_o + static_cast<int64_t>(row) * S * D;
+  *reinterpret_cast<float4*>(prow + static_cast<int64_t>(a.num_splits) * D + j) = ow;
+  if (tid == 0) a.part_lse[static_cast<int64_t>(row) * S + a.num_splits] = lse_w;
+  float4 acc = make_float4(ww * ow.x, ww * ow.y, ww * ow.z, ww * ow.w);
+#pragma unroll 4
+  for (int p = 0; p < a.num_splits; ++p) {
+    const float w = wts[p];
+    const float4 v = *reinterpret_cast<const float4*>(prow + static_cast<int64_t>(p) * D + j);
+    acc.x = w > 0.f ? fmaf(w, v.x, acc.x) : acc.x;
+    acc.y = w > 0.f ? fmaf(w, v.y, acc.y) : acc.y;
+    acc.z = w > 0.f ? fmaf(w, v.z, acc.z) : acc.z;
+    acc.w = w > 0.f ? fmaf(w, v.w, acc.w) : acc.w;
+  }
+  const __nv_bfloat162 o01 = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
+  const __nv_bfloat162 o23 = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
+  *reinterpret_cast<uint2*>(out + b * out_sb + h * out_sh + j) =
+      make_uint2(*reinterpret_cast<const uint32_t*>(&o01), *reinterpret_cast<const uint32_t*>(&o23));
+  if (tid == 0 && out_lse) out_lse[row] = den > 0.f ? mref + logf(den) : -INFINITY;
 }
 
 // ---- host side ---------------------------------------------------------------------------
@@ -825,9 +1045,44 @@ int launch_merge(const float* part_o, int64_t row_stride, int64_t part_stride, c
                  int64_t lse_row_stride, int64_t lse_part_stride, int n_parts, int64_t rows, int d,
                  uint16_t* out_bf16, float* out_f32, int64_t ld_out, float* out_lse, cudaStream_t s) {
   if (rows == 0) return ROLAQ_OK;
-  merge_kernel<<<static_cast<unsigned>(rows), 128, 0, s>>>(part_o, row_stride, part_stride, part_lse, lse_row_stride,
-                                                          lse_part_stride, n_parts, d, out_bf16, out_f32, ld_out,
-                                                          out_lse);
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const bool vec = d % 4 == 0 && row_stride % 4 == 0 && part_stride % 4 == 0 && a16(part_o) &&
+                   (out_f32 == nullptr || (a16(out_f32) && ld_out % 4 == 0)) &&
+                   (out_bf16 == nullptr || ((reinterpret_cast<uintptr_t>(out_bf16) & 7u) == 0 && ld_out % 4 == 0));
+  const int threads = d >= 512 ? 128 : 64;
+  const size_t smem = size_t(n_parts) * sizeof(float);
+  if (smem > 48 * 1024) return ROLAQ_EUNSUPPORTED;
+  if (vec)
+    merge_kernel<true><<<static_cast<unsigned>(rows), threads, smem, s>>>(
+        part_o, row_stride, part_stride, part_lse, lse_row_stride, lse_part_stride, n_parts, d, out_bf16, out_f32,
+        ld_out, out_lse);
+  else
+    merge_kernel<false><<<static_cast<unsigned>(rows), threads, smem, s>>>(
+        part_o, row_stride, part_stride, part_lse, lse_row_stride, lse_part_stride, n_parts, d, out_bf16, out_f32,
+        ld_out, out_lse);
+  return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;
+}
+
+// tcgen05 INT2 splits + the fused window/merge kernel, when the shape and the output
+// layout allow it (contiguous [B, H, D] partials, 8-byte aligned output rows); otherwise
+// ROLAQ_EUNSUPPORTED and the caller runs launch_decode + launch_merge.
+int launch_decode_merged(const DecodeArgs& a, int heads, uint16_t* out, int64_t out_sb, int64_t out_sh,
+                         float* out_lse, cudaStream_t s) {
+  if (!decode_tc_supported(a, heads)) return ROLAQ_EUNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(out) & 7u) || (out_sb & 3) || (out_sh & 3) ||
+      (reinterpret_cast<uintptr_t>(a.part_o) & 15u))
+    return ROLAQ_EUNSUPPORTED;
+  const int nw_cap = a.cache.sink + a.cache.recent;
+  const size_t smem = (size_t(nw_cap) * (512 + 64 + 1) + size_t(a.num_splits)) * sizeof(float);
+  if (smem > 200 * 1024) return ROLAQ_EUNSUPPORTED;
+  static const bool attr_ok = cudaFuncSetAttribute(merge_window_kernel<512, 64>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) ==
+                              cudaSuccess;
+  if (!attr_ok) return ROLAQ_ECUDA;
+  int rc = launch_decode_tc(a, s);
+  if (rc != ROLAQ_OK) return rc;
+  merge_window_kernel<512, 64><<<static_cast<unsigned>(int64_t(a.batch) * heads), 128, smem, s>>>(
+      a, heads, out, out_sb, out_sh, out_lse, nw_cap);
   return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;
 }
 

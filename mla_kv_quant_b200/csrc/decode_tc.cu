@@ -30,10 +30,10 @@
 //   * PV = kind::f8f6f4 (M = 128 latent elements of a group, N = 32, K = 128 tokens)
 //     accumulates straight into a TMEM O accumulator across all tiles.
 // When m_ref or E_g moves, each token warp rescales the O columns of its own heads in
-// TMEM (lane quarter = its tokens' quarter) and, at the end, writes those columns.  An
-// issuer warp does all MMA issue, the k_pe TMA and L2 prefetch, driven by mbarriers, so
-// the token warps never wait on one another's issue work: QK^T(i+1) is issued as soon
-// as its codes are in TMEM and PV(i) as soon as P'(i) is in shared memory.
+// TMEM (lane quarter = its tokens' quarter) and, at the end, writes those columns.  An MMA
+// warp issues QK^T(i+1) as soon as its codes are in TMEM and PV(i) as soon as P'(i) is in
+// shared memory; a producer warp keeps the k_pe TMA, the params bulk copies and the L2
+// prefetch ahead; all three roles are driven by mbarriers.
 #include "kernels.cuh"
 
 namespace rolaq {
@@ -41,9 +41,12 @@ namespace tc {
 
 constexpr int D = 512, DR = 64, H = 16, NG = 4;
 constexpr int TILE = 128, PAGE = 64;
-constexpr int NTOK_WARPS = 16;  // + one issuer warp (17 warps: at most 5 per SM sub-partition -> 96 registers)
+// 16 token warps + an MMA warp + a producer warp (18 warps: at most 5 per SM sub-partition
+// -> 96 registers); the MMA and producer warps sit on different sub-partitions.
+constexpr int NTOK_WARPS = 16;
 constexpr int TOK_THREADS = NTOK_WARPS * 32;
-constexpr int THREADS = TOK_THREADS + 32;
+constexpr int MMA_WARP = NTOK_WARPS, PROD_WARP = NTOK_WARPS + 1;
+constexpr int THREADS = TOK_THREADS + 64;
 // P' = 2^(s - m_ref) s_g E_g < 2^kTau * kEMax = 362 stays inside E4M3 (448).
 constexpr float kTau = 4.5f;    // m_ref moves when a tile max exceeds it by more than this (log2 units)
 constexpr float kEMax = 16.f;   // E_g moves when max_t s_tg * E_g reaches this (set to [4, 8))
@@ -75,7 +78,11 @@ constexpr int F_FINL = F_GMAX + 2 * NG * 4;  // [4][H]      sum P per token quar
 constexpr int F_FINY = F_FINL + 4 * H;       // [4][NG][H]  sum P' z per token quarter
 constexpr int F_TOTAL = F_FINY + 4 * NG * H;
 constexpr int OFF_BAR = OFF_F + ((F_TOTAL * 4 + 15) / 16) * 16;
-constexpr int B_KPE = 0, B_QK = 2, B_PV = 3, B_AQK = 4, B_PREADY = 5, B_PAR = 6, N_BARS = 8;
+// B_KFREE[s]: QK^T of the tile in k_pe stage s has completed (producer may refill it);
+// B_PFREE[s]: the token threads have read params stage s.  Per-stage barriers keep every
+// waiter within one phase of the barrier it waits on.
+constexpr int B_KPE = 0, B_QK = 2, B_PV = 3, B_AQK = 4, B_PREADY = 5, B_PAR = 6, B_KFREE = 8, B_PFREE = 10,
+              N_BARS = 12;
 constexpr int OFF_TMEMSLOT = OFF_BAR + N_BARS * 8;
 constexpr size_t SMEM = size_t(OFF_TMEMSLOT) + 16 + 1024;
 static_assert(SMEM <= 227 * 1024, "shared memory budget");
@@ -213,6 +220,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(&bars[B_PV], 1);
     mbar_init(&bars[B_AQK], TOK_THREADS);
     mbar_init(&bars[B_PREADY], TOK_THREADS);
+    for (int st = 0; st < 2; ++st) {
+      mbar_init(&bars[B_KFREE + st], 1);
+      mbar_init(&bars[B_PFREE + st], TOK_THREADS);
+    }
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -279,33 +290,31 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t id_qk = idesc_e4m3(128, 32, 0, 0);
   const uint32_t id_pe = idesc_bf16(128, 16);
   const uint32_t id_pv = idesc_e4m3(128, 32, 1, 1);
-  auto issue_qk = [&](int i) {
+  // Descriptors: a tile's operands sit at fixed offsets from a few bases; within 227 KB the
+  // start-address field (addr >> 4, 14 bits) never carries, so offsets are plain adds.
+  auto issue_qk = [&](int i, uint64_t dq0, uint64_t dk0, uint64_t dqp) {
 #pragma unroll
     for (int g = 0; g < NG; ++g) {
-      const uint32_t qb = smem_u32(smem + OFF_QB + g * QB_GROUP);
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk)
-        umma_f8_ts(tmem + T_DQK + 32 * g, tmem + T_AQK + 32 * g + 8 * kk, sw128_kmajor_desc(qb + 32 * kk), id_qk,
-                   kk > 0);
+        umma_f8_ts(tmem + T_DQK + 32 * g, tmem + T_AQK + 32 * g + 8 * kk,
+                   dq0 + static_cast<uint64_t>((QB_GROUP >> 4) * g + 2 * kk), id_qk, kk > 0);
     }
-    const uint32_t ka = smem_u32(smem + OFF_KPE + (i & 1) * KPE_STAGE);
-    const uint32_t kb = smem_u32(smem + OFF_QPE);
+    const uint64_t dk = dk0 + static_cast<uint64_t>((i & 1) * (KPE_STAGE >> 4));
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk)
-      umma_bf16_ss(tmem + T_DPE, sw128_kmajor_desc(ka + 32 * kk), sw128_kmajor_desc(kb + 32 * kk), id_pe, kk > 0);
+    for (int kk = 0; kk < 4; ++kk) umma_bf16_ss(tmem + T_DPE, dk + 2 * kk, dqp + 2 * kk, id_pe, kk > 0);
     umma_commit(&bars[B_QK]);
+    umma_commit(&bars[B_KFREE + (i & 1)]);
   };
-
-  auto issue_pv = [&](int i) {
-    const int s = i & 1;
+  auto issue_pv = [&](int i, uint64_t dpa0, uint64_t dpb0) {
+    const uint64_t da = dpa0 + static_cast<uint64_t>((i & 1) * (PVA_BUF >> 4));
+    const uint64_t db = dpb0 + static_cast<uint64_t>((i & 1) * (PB_BUF >> 4));
 #pragma unroll
     for (int g = 0; g < NG; ++g) {
-      const uint32_t pa = smem_u32(smem + OFF_PVA + s * PVA_BUF + g * PVA_GROUP);
-      const uint32_t pbb = smem_u32(smem + OFF_PB + s * PB_BUF + g * PB_GROUP);
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk)
-        umma_f8_ss(tmem + T_O + 32 * g, mn_major_desc(pa + 4096 * kk, 128), mn_major_desc(pbb + 1024 * kk, 32),
-                   id_pv, (i > 0 || kk > 0) ? 1u : 0u);
+        umma_f8_ss(tmem + T_O + 32 * g, da + static_cast<uint64_t>((PVA_GROUP >> 4) * g + 256 * kk),
+                   db + static_cast<uint64_t>((PB_GROUP >> 4) * g + 64 * kk), id_pv, (i > 0 || kk > 0) ? 1u : 0u);
     }
     umma_commit(&bars[B_PV]);
   };
@@ -435,6 +444,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int j = 0; j < 4; ++j)
           s2[j] = ok ? fmaf(A[j], kinv[j], __uint_as_float(pe[j]) - B[j]) * sl2 : -INFINITY;
       }
+      mbar_arrive(&bars[B_PFREE + s]);  // params stage s has been read (sc, zz are in registers)
       // -- 1b. codes of tile i+1 into TMEM (QK^T(i) has completed) --
       if (i + 1 < ntiles) {
         const uint4 cws[2] = {cw0, cw1};
@@ -550,9 +560,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         *reinterpret_cast<uint2*>(pb + g * PB_GROUP + sw32(t, 8 * k)) = make_uint2(hw, lw);
       }
       fence_proxy_async();
-      // -- 4. the PV-A tile of i+1 into buffer (i+1) & 1, last read by PV(i-1) --
+      // -- 4. the PV-A tile of i+1 into buffer (i+1) & 1, last read by PV(i-1).  PV(i-1) is
+      //       waited for on every tile (the last one too): PREADY(i) then cannot complete
+      //       before the MMA warp has taken PREADY(i-1), so its parity wait never aliases. --
+      if (alive && i >= 1) alive = mbar_wait(&bars[B_PV], (i - 1) & 1, a.err);
       if (i + 1 < ntiles) {
-        if (alive && i >= 1) alive = mbar_wait(&bars[B_PV], (i - 1) & 1, a.err);
         uint32_t r[32];
         expand(r);
         store_pva((i + 1) & 1, r);
@@ -618,8 +630,31 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
     tc_fence_before();
+  } else if (warp == MMA_WARP) {
+    if (lane == 0) {
+      // ---- MMA issue: QK^T(i) once its codes are in TMEM, PV(i-1) once P'(i-1) is ready -------
+      const uint64_t dq0 = sw128_kmajor_desc(smem_u32(smem + OFF_QB));
+      const uint64_t dk0 = sw128_kmajor_desc(smem_u32(smem + OFF_KPE));
+      const uint64_t dqp = sw128_kmajor_desc(smem_u32(smem + OFF_QPE));
+      const uint64_t dpa0 = mn_major_desc(smem_u32(smem + OFF_PVA), 128);
+      const uint64_t dpb0 = mn_major_desc(smem_u32(smem + OFF_PB), 32);
+      for (int i = 0; i < ntiles; ++i) {
+        if (alive) alive = mbar_wait(&bars[B_AQK], i & 1, a.err);
+        if (alive) alive = mbar_wait(&bars[B_KPE + (i & 1)], (i >> 1) & 1, a.err);
+        tc_fence_after();
+        issue_qk(i, dq0, dk0, dqp);
+        if (i >= 1) {
+          if (alive) alive = mbar_wait(&bars[B_PREADY], (i - 1) & 1, a.err);
+          tc_fence_after();
+          issue_pv(i - 1, dpa0, dpb0);
+        }
+      }
+      if (alive) alive = mbar_wait(&bars[B_PREADY], (ntiles - 1) & 1, a.err);
+      tc_fence_after();
+      issue_pv(ntiles - 1, dpa0, dpb0);
+    }
   } else if (lane == 0) {
-    // ---- issuer: k_pe TMA, L2 prefetch, QK^T and PV issue --------------------------------------
+    // ---- producer: k_pe TMA and params bulk copies into their 2-stage rings, L2 prefetch -----
     prefetch_tensormap(&tm_rope);
     // page ids of tiles i+1 .. i+5, fetched five tiles ahead
     int32_t r1a = page_raw(1, 0), r1b = page_raw(1, 1), r2a = page_raw(2, 0), r2b = page_raw(2, 1);
@@ -637,18 +672,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (ntiles > 2) prefetch_tile(2, r2a, r2b);
     if (ntiles > 3) prefetch_tile(3, r3a, r3b);
     for (int i = 0; i < ntiles; ++i) {
-      if (alive) alive = mbar_wait(&bars[B_AQK], i & 1, a.err);
-      if (alive) alive = mbar_wait(&bars[B_KPE + (i & 1)], (i >> 1) & 1, a.err);
-      tc_fence_after();
-      issue_qk(i);
-      if (i >= 1) {
-        if (alive) alive = mbar_wait(&bars[B_PREADY], (i - 1) & 1, a.err);
-        tc_fence_after();
-        issue_pv(i - 1);
-        if (i + 1 < ntiles) issue_params(i + 1, r1a, r1b);  // stage (i+1) & 1 held tile i-1, read before P'(i-1)
+      if (i + 1 < ntiles && i >= 1) {  // params stage (i+1) & 1 held tile i-1
+        if (alive) alive = mbar_wait(&bars[B_PFREE + ((i - 1) & 1)], ((i - 1) >> 1) & 1, a.err);
+        issue_params(i + 1, r1a, r1b);
       }
-      if (i + 2 < ntiles) {  // stage i & 1 is free once QK^T(i) has completed
-        if (alive) alive = mbar_wait(&bars[B_QK], i & 1, a.err);
+      if (i + 2 < ntiles) {  // k_pe stage i & 1 is free once QK^T(i) has completed
+        if (alive) alive = mbar_wait(&bars[B_KFREE + (i & 1)], (i >> 1) & 1, a.err);
         issue_kpe(i + 2, r2a, r2b);
       }
       if (i + 4 < ntiles) prefetch_tile(i + 4, r4a, r4b);
@@ -656,9 +685,6 @@ __global__ void __launch_bounds__(THREADS, 1)
       r5a = page_raw(i + 6, 0);
       r5b = page_raw(i + 6, 1);
     }
-    if (alive) alive = mbar_wait(&bars[B_PREADY], (ntiles - 1) & 1, a.err);
-    tc_fence_after();
-    issue_pv(ntiles - 1);
   }
 
   __syncthreads();

@@ -73,6 +73,10 @@ int launch_prepare_splits(const int32_t* splits, int32_t* quant, int32_t* merge,
 
 // decode.cu
 int launch_decode(const DecodeArgs& a, int heads, cudaStream_t s);
+// INT2 splits and the window/merge in one go where the fused kernels apply (D/Dr/H =
+// 512/64/16, aligned output); ROLAQ_EUNSUPPORTED otherwise (nothing launched).
+int launch_decode_merged(const DecodeArgs& a, int heads, uint16_t* out, int64_t out_sb, int64_t out_sh,
+                         float* out_lse, cudaStream_t s);
 int launch_merge(const float* part_o, int64_t row_stride, int64_t part_stride, const float* part_lse,
                  int64_t lse_row_stride, int64_t lse_part_stride, int n_parts, int64_t rows, int d,
                  uint16_t* out_bf16, float* out_f32, int64_t ld_out, float* out_lse, cudaStream_t s);
