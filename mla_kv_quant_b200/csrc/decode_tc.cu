@@ -116,6 +116,12 @@ __device__ __forceinline__ float group_e(float gm) {
 
 __device__ __forceinline__ float max4(float4 v) { return fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)); }
 
+// a / b for powers of two a <= b in the normal range (exact by exponent arithmetic; a ratio
+// below 2^-126 becomes 2^-126, which only arises when the accumulator it scales is empty).
+__device__ __forceinline__ float pow2_ratio(float a, float b) {
+  return __int_as_float(max(__float_as_int(a) - __float_as_int(b) + (127 << 23), 1 << 23));
+}
+
 // K index (position in a row of FP8 operand bytes) <-> element of the group; an involution.
 __device__ __forceinline__ int kperm(int w) { return (w & ~15) | ((w & 3) << 2) | ((w >> 2) & 3); }
 
@@ -501,12 +507,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         resc |= up;
       }
 #pragma unroll
-      for (int g = 0; g < NG; ++g) {
-        const float en = group_e(gm[g]);
-        const bool up = i > 0 && gm[g] * E[g] >= kEMax;
-        gf[g] = up ? en / E[g] : 1.f;
-        E[g] = (i == 0 || up) ? en : E[g];
-        resc |= up;
+      for (int g = 0; g < NG; ++g) {  // branches are uniform: every thread sees the same tables
+        gf[g] = 1.f;
+        if (i == 0) {
+          E[g] = group_e(gm[g]);
+        } else if (gm[g] * E[g] >= kEMax) {
+          const float en = group_e(gm[g]);
+          gf[g] = pow2_ratio(en, E[g]);
+          E[g] = en;
+          resc = true;
+        }
       }
       if (resc) {
 #pragma unroll
