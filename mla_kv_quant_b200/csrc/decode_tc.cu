@@ -574,9 +574,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       //       waited for on every tile (the last one too): PREADY(i) then cannot complete
       //       before the MMA warp has taken PREADY(i-1), so its parity wait never aliases. --
       if (alive && i >= 1) alive = mbar_wait(&bars[B_PV], (i - 1) & 1, a.err);
+      __syncwarp();  // the tcgen05.ld below is warp-collective
       if (i + 1 < ntiles) {
-        uint32_t r[32];
-        expand(r);
+        uint32_t r[32];  // the FP8 codes of tile i+1, as 1b wrote them to TMEM
+        tc_fence_after();
+        tmem_ld32(tmem + lane_base + T_AQK + 32 * k, r);
+        tmem_wait_ld();
+        reg_fence(r);
+        tc_fence_before();
         store_pva((i + 1) & 1, r);
         ok = ok_next;
         if (i + 2 < ntiles) {
