@@ -805,21 +805,34 @@ __global__ void merge_kernel(const float* __restrict__ part_o, int64_t row_strid
   if (threadIdx.x == 0 && out_lse) out_lse[row] = den > 0.f ? mref + logf(den) : -INFINITY;
 }
 
-// Window split + LSE merge for the tcgen05 path, one CTA per (request, head): the window
-// rows are gathered once per CTA (lookups by one thread per row, 16-byte loads by a warp per
-// row), scored against this head's query (a warp per row, lanes over the 576 elements, a
-// shuffle sum), softmaxed, and their partial is merged with the num_splits INT2 partials the
-// tcgen05 kernel wrote.  The window partial is also stored in split num_splits of
-// part_o / part_lse, so the scratch holds every partial after the call as before.
+// Window split + LSE merge for the tcgen05 path, one CTA per (request, head) and no
+// shared-memory copy of the rows (so that every CTA of a launch is resident at once): a
+// warp per window row computes the score (lane l owns elements 4l + 128u + c and the rope
+// elements 4l + c), warp 0 the softmax, then each thread re-reads its 4 elements of every
+// row (L1-resident by then) for the window partial and merges it with the num_splits INT2
+// partials the tcgen05 kernel wrote.  The window partial is also stored in split
+// num_splits of part_o / part_lse, so the scratch holds every partial after the call.
+template <int D, int DR>
+__device__ __forceinline__ void window_elems4(const DecodeArgs& a, int64_t slot, int64_t r, int e0, float (&v)[4]) {
+  if (r >= 0) {
+    const uint2 w = *reinterpret_cast<const uint2*>(a.cache.hp + r * D + e0);
+    v[0] = __uint_as_float(w.x << 16);
+    v[1] = __uint_as_float(w.x & 0xFFFF0000u);
+    v[2] = __uint_as_float(w.y << 16);
+    v[3] = __uint_as_float(w.y & 0xFFFF0000u);
+  } else {
+    const uint32_t cb = a.cache.codes[slot * (D / 4) + e0 / 4];
+    const float2 sz = reinterpret_cast<const float2*>(a.cache.params)[slot * (D / 128) + e0 / 128];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) v[c] = __fmul_rn(__fsub_rn(static_cast<float>((cb >> (2 * c)) & 3u), sz.y), sz.x);
+  }
+}
+
 template <int D, int DR>
 __global__ void __launch_bounds__(128) merge_window_kernel(const DecodeArgs a, int heads, uint16_t* __restrict__ out,
-                                                           int64_t out_sb, int64_t out_sh, float* __restrict__ out_lse,
-                                                           int nw_cap) {
-  constexpr int KW = D + DR, KP = KW + 1;
-  static_assert(D == 4 * 128, "four outputs per thread");
-  extern __shared__ float dyn[];
-  float* kw = dyn;                 // [nw_cap][KP]
-  float* wts = kw + nw_cap * KP;   // [num_splits]
+                                                           int64_t out_sb, int64_t out_sh, float* __restrict__ out_lse) {
+  static_assert(D == 4 * 128 && DR == 64, "four latent elements per thread, 16 rope lanes");
+  extern __shared__ float wts[];  // [num_splits]
   __shared__ float sc[kMaxWindow];
   __shared__ int64_t rslot[kMaxWindow], rrow[kMaxWindow];
   __shared__ float stat[4];
@@ -840,7 +853,9 @@ __global__ void __launch_bounds__(128) merge_window_kernel(const DecodeArgs a, i
   const int s1 = min(max(rs, 0), lo), e1 = max(min(re, lo), s1);
   const int s2 = min(max(rs, hs), L), e2 = max(min(re, L), s2);
   const int n1 = e1 - s1;
-  const int nw = n1 + (e2 - s2);  // <= sink + recent = nw_cap
+  const int nw = n1 + (e2 - s2);  // <= sink + recent <= kMaxWindow (checked by the host)
+  if (tid == 32)  // the INT2 partials of this row are read last: start them towards L2 now
+    prefetch_l2(a.part_o + static_cast<int64_t>(row) * S * D, static_cast<uint32_t>(a.num_splits * D * 4));
   if (tid < nw) {
     const int pos = tid < n1 ? s1 + tid : s2 + (tid - n1);
     const int64_t page = a.page_table[b * a.pt_stride + pos / kPage];
@@ -855,65 +870,51 @@ __global__ void __launch_bounds__(128) merge_window_kernel(const DecodeArgs a, i
     rslot[tid] = slot;
     rrow[tid] = r;
   }
-  // this head's query, 18 elements per lane (e = lane + 32 u)
-  constexpr int QE = KW / 32;
-  static_assert(KW % 32 == 0, "query slice per lane");
-  float qv[QE];
-  {
-    const uint16_t* qh = a.q + b * a.q_sb + h * a.q_sh;
+  // this head's query at the lane's elements
+  const uint16_t* qh = a.q + b * a.q_sb + h * a.q_sh;
+  float qv[16], qr[4];
 #pragma unroll
-    for (int u = 0; u < QE; ++u) qv[u] = bf16f(qh[lane + 32 * u]);
+  for (int u = 0; u < 4; ++u) {
+    const uint2 w = *reinterpret_cast<const uint2*>(qh + 4 * lane + 128 * u);
+    qv[4 * u] = __uint_as_float(w.x << 16);
+    qv[4 * u + 1] = __uint_as_float(w.x & 0xFFFF0000u);
+    qv[4 * u + 2] = __uint_as_float(w.y << 16);
+    qv[4 * u + 3] = __uint_as_float(w.y & 0xFFFF0000u);
+  }
+  {
+    const uint2 w = lane < DR / 4 ? *reinterpret_cast<const uint2*>(qh + D + 4 * lane) : make_uint2(0, 0);
+    qr[0] = __uint_as_float(w.x << 16);
+    qr[1] = __uint_as_float(w.x & 0xFFFF0000u);
+    qr[2] = __uint_as_float(w.y << 16);
+    qr[3] = __uint_as_float(w.y & 0xFFFF0000u);
   }
   __syncthreads();
-  for (int p = warp; p < nw; p += 4) {
+  for (int p = warp; p < nw; p += 4) {  // scores: a warp per row
     const int64_t slot = rslot[p], r = rrow[p];
-    float* dst = kw + p * KP;
-    if (slot < 0) {
-      for (int e = lane; e < KW; e += 32) dst[e] = 0.f;
-    } else {
-      if (r >= 0) {
+    float acc = 0.f;
+    if (slot >= 0) {
 #pragma unroll
-        for (int u = 0; u < D / 256; ++u) {
-          const int e0 = 8 * lane + 256 * u;
-          const uint4 w = *reinterpret_cast<const uint4*>(a.cache.hp + r * D + e0);
-          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+      for (int u = 0; u < 4; ++u) {
+        float v[4];
+        window_elems4<D, DR>(a, slot, r, 4 * lane + 128 * u, v);
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            dst[e0 + 2 * v] = __uint_as_float(ws[v] << 16);
-            dst[e0 + 2 * v + 1] = __uint_as_float(ws[v] & 0xFFFF0000u);
-          }
-        }
-      } else {
-        for (int e0 = 16 * lane; e0 < D; e0 += 16 * 32) {
-          const uint32_t cw = *reinterpret_cast<const uint32_t*>(a.cache.codes + slot * (D / 4) + e0 / 4);
-          const float2 sz = reinterpret_cast<const float2*>(a.cache.params)[slot * (D / 128) + e0 / 128];
-#pragma unroll
-          for (int v = 0; v < 16; ++v)
-            dst[e0 + v] = __fmul_rn(__fsub_rn(static_cast<float>((cw >> (2 * v)) & 3u), sz.y), sz.x);
-        }
+        for (int c = 0; c < 4; ++c) acc = fmaf(qv[4 * u + c], v[c], acc);
       }
-      if (lane < DR / 8) {
-        const uint4 w = *reinterpret_cast<const uint4*>(a.cache.rope + slot * DR + 8 * lane);
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          dst[D + 8 * lane + 2 * v] = __uint_as_float(ws[v] << 16);
-          dst[D + 8 * lane + 2 * v + 1] = __uint_as_float(ws[v] & 0xFFFF0000u);
-        }
+      if (lane < DR / 4) {
+        const uint2 w = *reinterpret_cast<const uint2*>(a.cache.rope + slot * DR + 4 * lane);
+        acc = fmaf(qr[0], __uint_as_float(w.x << 16), acc);
+        acc = fmaf(qr[1], __uint_as_float(w.x & 0xFFFF0000u), acc);
+        acc = fmaf(qr[2], __uint_as_float(w.y << 16), acc);
+        acc = fmaf(qr[3], __uint_as_float(w.y & 0xFFFF0000u), acc);
       }
     }
-    __syncwarp();
-    float acc = 0.f;
-#pragma unroll
-    for (int u = 0; u < QE; ++u) acc = fmaf(qv[u], dst[lane + 32 * u], acc);
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
     if (lane == 0) sc[p] = acc * a.sm_scale;
   }
-  // INT2 part weights need only the LSEs: warp 1 prepares them while warp 0 does the window softmax
   __syncthreads();
   const float* lse_row = a.part_lse + static_cast<int64_t>(row) * S;
-  if (warp == 0) {
+  if (warp == 0) {  // window softmax
     const float x = lane < nw ? sc[lane] : -INFINITY;
     float m = x;
 #pragma unroll
@@ -927,7 +928,7 @@ __global__ void __launch_bounds__(128) merge_window_kernel(const DecodeArgs a, i
       stat[0] = nw > 0 ? m + logf(l) : -INFINITY;  // window lse
       stat[1] = l;
     }
-  } else if (warp == 1) {
+  } else if (warp == 1) {  // max of the INT2 partials' lse
     float m = -INFINITY;
     for (int p = lane; p < a.num_splits; p += 32) m = fmaxf(m, lse_row[p]);
 #pragma unroll
@@ -938,30 +939,31 @@ __global__ void __launch_bounds__(128) merge_window_kernel(const DecodeArgs a, i
   const float lse_w = stat[0], lw = stat[1];
   const float mref0 = fmaxf(stat[2], lse_w);
   const float mref = mref0 == -INFINITY ? 0.f : mref0;
-  float den = 0.f;  // every thread sums the same weights in the same order
   for (int p = tid; p < a.num_splits; p += blockDim.x) wts[p] = __expf(lse_row[p] - mref);
+  // window partial of this thread's 4 elements (rows re-read: L1 hits)
+  const int j = 4 * tid;
+  float ow[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int p = 0; p < nw; ++p) {
+    const int64_t slot = rslot[p];
+    if (slot < 0) continue;
+    float v[4];
+    window_elems4<D, DR>(a, slot, rrow[p], j, v);
+    const float e = sc[p];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) ow[c] = fmaf(e, v[c], ow[c]);
+  }
   __syncthreads();
+  float den = 0.f;  // every thread sums the same weights in the same order
   for (int p = 0; p < a.num_splits; ++p) den += wts[p];
   const float ww = lse_w == -INFINITY ? 0.f : __expf(lse_w - mref);
   den += ww;
   const float inv = den > 0.f ? 1.f / den : 0.f;
-  // window partial (this thread's 4 elements), stored as split num_splits, then the merge
-  const int j = 4 * tid;
-  float4 ow = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int p = 0; p < nw; ++p) {
-    const float e = sc[p];
-    const float* k = kw + p * KP + j;
-    ow.x = fmaf(e, k[0], ow.x);
-    ow.y = fmaf(e, k[1], ow.y);
-    ow.z = fmaf(e, k[2], ow.z);
-    ow.w = fmaf(e, k[3], ow.w);
-  }
   const float il = nw > 0 ? 1.f / lw : 0.f;
-  ow = make_float4(ow.x * il, ow.y * il, ow.z * il, ow.w * il);
+  const float4 o4 = make_float4(ow[0] * il, ow[1] * il, ow[2] * il, ow[3] * il);
   float* prow = a.part_o + static_cast<int64_t>(row) * S * D;
-  *reinterpret_cast<float4*>(prow + static_cast<int64_t>(a.num_splits) * D + j) = ow;
+  *reinterpret_cast<float4*>(prow + static_cast<int64_t>(a.num_splits) * D + j) = o4;
   if (tid == 0) a.part_lse[static_cast<int64_t>(row) * S + a.num_splits] = lse_w;
-  float4 acc = make_float4(ww * ow.x, ww * ow.y, ww * ow.z, ww * ow.w);
+  float4 acc = make_float4(ww * o4.x, ww * o4.y, ww * o4.z, ww * o4.w);
 #pragma unroll 4
   for (int p = 0; p < a.num_splits; ++p) {
     const float w = wts[p];
@@ -1072,17 +1074,12 @@ int launch_decode_merged(const DecodeArgs& a, int heads, uint16_t* out, int64_t 
   if ((reinterpret_cast<uintptr_t>(out) & 7u) || (out_sb & 3) || (out_sh & 3) ||
       (reinterpret_cast<uintptr_t>(a.part_o) & 15u))
     return ROLAQ_EUNSUPPORTED;
-  const int nw_cap = a.cache.sink + a.cache.recent;
-  const size_t smem = (size_t(nw_cap) * (512 + 64 + 1) + size_t(a.num_splits)) * sizeof(float);
-  if (smem > 200 * 1024) return ROLAQ_EUNSUPPORTED;
-  static const bool attr_ok = cudaFuncSetAttribute(merge_window_kernel<512, 64>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) ==
-                              cudaSuccess;
-  if (!attr_ok) return ROLAQ_ECUDA;
+  const size_t smem = size_t(a.num_splits) * sizeof(float);
+  if (smem > 48 * 1024) return ROLAQ_EUNSUPPORTED;
   int rc = launch_decode_tc(a, s);
   if (rc != ROLAQ_OK) return rc;
   merge_window_kernel<512, 64><<<static_cast<unsigned>(int64_t(a.batch) * heads), 128, smem, s>>>(
-      a, heads, out, out_sb, out_sh, out_lse, nw_cap);
+      a, heads, out, out_sb, out_sh, out_lse);
   return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;
 }
 
