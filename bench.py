@@ -349,7 +349,7 @@ def run_ours(args, rank, world, dev):
         "e2e": {"value": world * batch / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_s * 1e3,
                 "path": "try_fast_decode_store + packed_mla_decode_gf_fwd, eager, pinned host buffers"},
-        "roofline": {"kernel": "rolaq decode (decode_tc_kernel + window_rows_kernel + merge_kernel), one layer", "bound": "hbm",
+        "roofline": {"kernel": "rolaq decode (decode_tc_kernel + merge_window_kernel), one layer", "bound": "hbm",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_source": f"{peak_kind} hbm_gbs", "traffic": read_traffic(),
                      "algorithmic_bytes_per_launch": dbytes, "launch_us": dec_s * 1e6},

@@ -9,8 +9,8 @@ for one DeepSeek-V2-Lite request.  Every rank then merges the ``world`` partials
 with the same LSE kernel and holds the full output.
 
 The reference serves one GPU only (``deployment/serve.py:135-136``); this module
-is the multi-GPU extension the packed path's sharding needs.  No cluster multicast
-and no remote TMA is involved: the partials cross NVLink through NCCL.
+is the multi-GPU extension the packed path's sharding needs.  No kernel reads
+another GPU's memory: the partials cross NVLink through NCCL.
 """
 
 from __future__ import annotations
