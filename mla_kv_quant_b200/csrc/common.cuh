@@ -399,4 +399,54 @@ __device__ __forceinline__ uint32_t lloyd_code(float diff, float std_, float t) 
   return static_cast<uint32_t>(n >= -t) + static_cast<uint32_t>(n >= 0.f) + static_cast<uint32_t>(n >= t);
 }
 
+// Neighbouring FP32 values (towards -inf / +inf), zeros included.
+__device__ __forceinline__ float f32_prev(float d) {
+  const int b = __float_as_int(d);
+  if ((b & 0x7FFFFFFF) == 0) return __int_as_float(0x80000001);
+  return __int_as_float(d > 0.f ? b - 1 : b + 1);
+}
+__device__ __forceinline__ float f32_next(float d) {
+  const int b = __float_as_int(d);
+  if ((b & 0x7FFFFFFF) == 0) return __int_as_float(0x00000001);
+  return __int_as_float(d > 0.f ? b + 1 : b - 1);
+}
+
+// The smallest FP32 d with RN(d / std_) >= c, for finite std_ > 0.  RN(d / std_) does
+// not decrease as d grows, so [RN(diff / std_) >= c] == [diff >= bound] for every diff:
+// the Lloyd code [n >= -t] + [n >= 0] + [n >= t] becomes three compares per element with
+// the reference's IEEE-quotient semantics.  Returns false if the search did not settle
+// (then the caller falls back to the per-element quotient).
+__device__ __forceinline__ bool quotient_bound(float c, float std_, float* bound) {
+  float d = __fmul_rn(c, std_);
+  if (__fdiv_rn(d, std_) >= c) {
+#pragma unroll 1
+    for (int k = 0; k < 16; ++k) {
+      const float p = f32_prev(d);
+      if (!(__fdiv_rn(p, std_) >= c)) {
+        *bound = d;
+        return true;
+      }
+      d = p;
+    }
+  } else {
+#pragma unroll 1
+    for (int k = 0; k < 16; ++k) {
+      d = f32_next(d);
+      if (__fdiv_rn(d, std_) >= c) {
+        *bound = d;
+        return true;
+      }
+    }
+  }
+  return false;
+}
+
+// The smallest FP32 d with RN(d / std_) >= 0, for 0 < std_ < 2^24: d / std_ rounds to -0
+// exactly when |d| = k * 2^-149 with k <= std_ / 2 (ties to even give 0), so the bound is
+// -floor(std_ / 2) * 2^-149, a denormal (or -0 when std_ < 2).
+__device__ __forceinline__ float quotient_bound_zero(float std_) {
+  const uint32_t k = static_cast<uint32_t>(floorf(__fmul_rn(std_, 0.5f)));
+  return __int_as_float(static_cast<int>(0x80000000u | k));
+}
+
 }  // namespace rolaq

@@ -57,6 +57,29 @@ __device__ __forceinline__ RowMeta row_meta(const WriterArgs& a, int64_t row) {
   return m;
 }
 
+// Codes of one (row, 128-group) from the IEEE quotient per element: the reference's
+// definition, used when the per-group bounds do not apply.  Warp-collective (TMEM loads);
+// kept out of line so that the common path stays small.
+__device__ __noinline__ void exact_code_words(uint32_t taddr, float mean, float stdv, float thr, uint32_t* words) {
+  uint32_t r[32];
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    tmem_ld32(taddr + c * 32, r);
+    tmem_wait_ld();
+    uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const uint32_t code = lloyd_code(__fsub_rn(__uint_as_float(r[j]), mean), stdv, thr);
+      if (j < 16)
+        w0 |= code << (2 * j);
+      else
+        w1 |= code << (2 * (j - 16));
+    }
+    words[2 * c] = w0;
+    words[2 * c + 1] = w1;
+  }
+}
+
 template <bool kPlain>
 __global__ void __launch_bounds__(kWriterThreads, 1)
     writer_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
@@ -243,47 +266,40 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
         }
         const float var = __fmul_rn(acc.total(), 1.0f / 128.0f);
         const float stdv = __fsqrt_rn(__fadd_rn(var, 1e-8f));
-        const float rstd = __frcp_rn(stdv);
         const float thr = args.codec.threshold;
-        const bool exact_all = !(stdv < 1e30f);
-        // pass 3: codes.  n ~= diff * (1/std) decides every element whose |n| is not
-        // within 2^-20 relative of t; the rest use the IEEE quotient diff / std, which
-        // is what the reference compares.
+        // pass 3: codes.  n = RN(diff / std) never decreases as diff grows, so each of the
+        // reference's tests [n >= -t], [n >= 0], [n >= t] is diff >= an exact FP32 bound
+        // found once per (row, group) with the IEEE quotient (the middle one in closed form);
+        // a std of 2^24 or more, or a bound search that does not settle, takes the
+        // per-element quotient instead.
+        float b_lo = 0.f, b_mid = 0.f, b_hi = 0.f;
+        bool exact_all = !(stdv < 16777216.f);
+        if (!exact_all) {
+          b_mid = quotient_bound_zero(stdv);
+          exact_all = !(quotient_bound(-thr, stdv, &b_lo) && quotient_bound(thr, stdv, &b_hi));
+        }
         uint32_t words[8];
+        if (__any_sync(0xFFFFFFFFu, exact_all)) {
+          exact_code_words(taddr, mean, stdv, thr, words);  // rare: the whole warp, quotient per element
+        } else {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld32(taddr + c * 32, r);
-          tmem_wait_ld();
-          uint32_t w0 = 0, w1 = 0;
-          bool amb = false;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float df = __fsub_rn(__uint_as_float(r[j]), mean);
-            const float a = fabsf(__fmul_rn(df, rstd));
-            const uint32_t hi = (__float_as_uint(df) >> 31) ^ 1u;  // df >= 0 (also -0.0)
-            const uint32_t lo = hi ^ static_cast<uint32_t>(a < thr);
-            amb |= fabsf(a - thr) <= a * 9.5367431640625e-07f || a < 1e-30f;
-            const uint32_t code = (hi << 1) | lo;
-            if (j < 16)
-              w0 |= code << (2 * j);
-            else
-              w1 |= code << (2 * (j - 16));
-          }
-          if (amb || exact_all) {
-            w0 = 0;
-            w1 = 0;
+          for (int c = 0; c < 4; ++c) {
+            tmem_ld32(taddr + c * 32, r);
+            tmem_wait_ld();
+            uint32_t w0 = 0, w1 = 0;
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const float df = __fsub_rn(__uint_as_float(r[j]), mean);
-              const uint32_t code = lloyd_code(df, stdv, thr);
+              const uint32_t code = static_cast<uint32_t>(df >= b_lo) + static_cast<uint32_t>(df >= b_mid) +
+                                    static_cast<uint32_t>(df >= b_hi);
               if (j < 16)
                 w0 |= code << (2 * j);
               else
                 w1 |= code << (2 * (j - 16));
             }
+            words[2 * c] = w0;
+            words[2 * c + 1] = w1;
           }
-          words[2 * c] = w0;
-          words[2 * c + 1] = w1;
         }
         const float scale = __fmul_rn(args.codec.scale_factor, stdv);
         const float zero = __fsub_rn(args.codec.zero_const, __fdiv_rn(mean, scale));
