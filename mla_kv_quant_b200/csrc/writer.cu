@@ -1,31 +1,35 @@
 // Fused packed-INT2 cache writer for sm_100a.
 //
 // c = c_kv @ R runs on tcgen05 tensor cores: BF16 operands are staged in shared
-// memory by TMA (128-byte swizzle), one elected thread issues kind::f16 MMAs into a
-// double-buffered FP32 accumulator in tensor memory, and eight epilogue warps read
-// the accumulator back (tcgen05.ld) to run the Lloyd INT2 codec, pack 4 codes per
-// byte, scatter codes/params by slot, and write k_pe and the s4r16 window rows.
+// memory by TMA (128-byte swizzle), one elected thread issues kind::f16 MMAs into one of
+// four FP32 accumulators in tensor memory, and four sets of four epilogue warps (one warp
+// per TMEM lane quarter) read the accumulators back (tcgen05.ld) to run the Lloyd INT2
+// codec, pack 4 codes per byte, scatter codes/params by slot, and write k_pe and the
+// s4r16 window rows.  Set s takes every fourth tile of the CTA, so the codec of four
+// tiles is in flight at once while the tensor core computes the next.
 //
 // Reference behaviour: deployment/sglang/QuantKernel/mla_fused_writer.py:54-224
 // (FP32 GEMM + Triton _pack_and_aux) and mla_quant/oscar.py:120-144 (codec).
 //
-// CTA tile: 128 rows x 256 latent columns (two 128-wide quantisation groups).  A row
-// of D = 512 is covered by two tiles; adjacent CTAs take the two halves of the same
-// rows so the second read of those rows hits L2.
+// CTA tile: 128 rows x 128 latent columns = one quantisation group.  A row of D = 512 is
+// covered by four tiles; adjacent CTAs take the groups of the same rows, so the repeated
+// reads of those rows hit L2.
 #include "kernels.cuh"
 
 namespace rolaq {
 
 constexpr int kTileM = 128;
-constexpr int kTileN = 256;
-constexpr int kTileK = 64;  // one 128-byte swizzle row of BF16
-constexpr int kStages = 4;
+constexpr int kTileN = 128;  // one quantisation group
+constexpr int kTileK = 64;   // one 128-byte swizzle row of BF16
+constexpr int kStages = 6;
 constexpr int kABytes = kTileM * kTileK * 2;  // 16 KB
-constexpr int kBBytes = kTileN * kTileK * 2;  // 32 KB
+constexpr int kBBytes = kTileN * kTileK * 2;  // 16 KB
 constexpr int kStageBytes = kABytes + kBBytes;
-constexpr int kWriterThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
-constexpr int kEpiThreads = 256;
-constexpr uint32_t kTmemCols = 512;  // two 256-column accumulators
+constexpr int kNumBuf = 4;                       // TMEM accumulators = epilogue warp sets
+constexpr int kEpiWarps = 4 * kNumBuf;           // one warp per TMEM lane quarter per set
+constexpr int kWriterThreads = 32 * (2 + kEpiWarps);  // warp 0 TMA, warp 1 MMA, warps 2.. epilogue
+constexpr int kSetThreads = 128;
+constexpr uint32_t kTmemCols = kNumBuf * kTileN;  // 512
 constexpr size_t kWriterSmem = size_t(kStages) * kStageBytes + 1024 + 256;
 
 // Per-row bookkeeping shared by the codec epilogue warps of one row.
@@ -90,16 +94,16 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
-  uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* tempty = tfull + kNumBuf;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + kNumBuf);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int d = args.d;
-  const int halves = d / kTileN;
+  const int groups = d / kTileN;
   const int64_t row_tiles = (args.n + kTileM - 1) / kTileM;
-  const int64_t tiles = row_tiles * halves;
+  const int64_t tiles = row_tiles * groups;
   const int kchunks = d / kTileK;
 
   if (threadIdx.x == 0) {
@@ -107,9 +111,9 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kNumBuf; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], kEpiThreads);
+      mbar_init(&tempty[b], kSetThreads);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -131,8 +135,8 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
-        const int32_t row0 = static_cast<int32_t>((t / halves) * kTileM);
-        const int32_t col0 = static_cast<int32_t>((t % halves) * kTileN);
+        const int32_t row0 = static_cast<int32_t>((t / groups) * kTileM);
+        const int32_t col0 = static_cast<int32_t>((t % groups) * kTileN);
         for (int kc = 0; kc < kchunks; ++kc) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, args.err)) {
             *abort_flag = 1;
@@ -159,8 +163,8 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
       const uint32_t idesc = idesc_bf16(kTileM, kTileN);
       int64_t lt = 0;
       for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++lt) {
-        const int buf = static_cast<int>(lt & 1);
-        const uint32_t use = static_cast<uint32_t>(lt >> 1);
+        const int buf = static_cast<int>(lt % kNumBuf);
+        const uint32_t use = static_cast<uint32_t>(lt / kNumBuf);
         if (!mbar_wait(&tempty[buf], (use & 1u) ^ 1u, args.err)) {
           *abort_flag = 1;
           break;
@@ -195,24 +199,25 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
       }
     }
   } else {
-    // ---- epilogue: 8 warps; warp w reads TMEM lanes 32*(w%4).. and group (w-2)/4 -----
+    // ---- epilogue: set (w-2)/4 takes tiles lt = set, set + 4, ...; warp w reads TMEM lanes
+    //      32*(w%4).. of accumulator lt % 4 -------------------------------------------------
     const int quad = warp & 3;
-    const int sub = (warp - 2) >> 2;
-    int64_t lt = 0;
-    for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++lt) {
-      const int buf = static_cast<int>(lt & 1);
-      const uint32_t use = static_cast<uint32_t>(lt >> 1);
+    const int set = (warp - 2) >> 2;
+    int64_t lt = set;
+    for (int64_t t = blockIdx.x + set * static_cast<int64_t>(gridDim.x); t < tiles;
+         t += kNumBuf * static_cast<int64_t>(gridDim.x), lt += kNumBuf) {
+      const int buf = static_cast<int>(lt % kNumBuf);
+      const uint32_t use = static_cast<uint32_t>(lt / kNumBuf);
       if (!mbar_wait(&tfull[buf], use & 1u, args.err)) {
         *abort_flag = 1;
         break;
       }
       tc_fence_after();
-      const int64_t row = (t / halves) * kTileM + quad * 32 + lane;
-      const int half = static_cast<int>(t % halves);
-      const int group = half * 2 + sub;  // global 128-column group index
+      const int64_t row = (t / groups) * kTileM + quad * 32 + lane;
+      const int group = static_cast<int>(t % groups);
       const bool valid = row < args.n;
       const uint32_t taddr =
-          tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(buf * kTileN + sub * 128);
+          tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(buf * kTileN);
       uint32_t r[32];
 
       if constexpr (kPlain) {
@@ -305,14 +310,14 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
         const float zero = __fsub_rn(args.codec.zero_const, __fdiv_rn(mean, scale));
         RowMeta m{0, -1, false};
         if (valid) m = row_meta(args, row);
-        if (valid && !m.ok && sub == 0 && half == 0) report(args.err, ROLAQ_DEV_BAD_SLOT);
+        if (valid && !m.ok && group == 0) report(args.err, ROLAQ_DEV_BAD_SLOT);
         if (valid && m.ok) {
           uint4* cdst = reinterpret_cast<uint4*>(args.cache.codes + m.slot * (d / 4) + group * 32);
           cdst[0] = make_uint4(words[0], words[1], words[2], words[3]);
           cdst[1] = make_uint4(words[4], words[5], words[6], words[7]);
           float2* pdst = reinterpret_cast<float2*>(args.cache.params + (m.slot * (d / 128) + group) * 2);
           *pdst = make_float2(scale, zero);
-          if (sub == 0 && half == 0 && m.slot > 0) {
+          if (group == 0 && m.slot > 0) {
             // k_pe and the slot <-> ring maps, once per row
             if (args.k_pe != nullptr) {
               const int dr = args.cache.rope_dim;
