@@ -507,10 +507,82 @@ def profile_layer(args, what):
                           "flops": 2.0 * n * D * D}))
 
 
+def run_seqsplit(args, rank, world, dev):
+    """Config 4b: one request of ``ctx`` tokens (131072 unless --ctx says otherwise) whose
+    pages are split into contiguous page-aligned slices over the ranks.  Per layer: each
+    rank decodes its slice (INT2 splits + window rows inside the slice, local LSE merge to
+    FP32), one NCCL all-gather of the (o, lse) partials, the same merge kernel.  Latency is
+    the max over ranks, timed with CUDA events; printed by rank 0 as one JSON line."""
+    from mla_kv_quant_b200 import ops, synth
+    from mla_kv_quant_b200.pool import PackedLatentPool
+    from mla_kv_quant_b200.seqsplit import gather_merge, rank_token_range
+
+    ctx = args.ctx if args.ctx != 16384 else 131072
+    start, end = rank_token_range(ctx, world, rank)
+    pt, num_slots = synth.page_table(1, ctx, seed=4, device=dev)
+    pool = PackedLatentPool(num_slots, 1, D, DR, max_reqs=1, sink=SINK, recent=RECENT, device=dev,
+                            rotations={0: synth.rotation(D, 1000)}, quantizer_params=[(0.85, synth.signal_gain(0.85))])
+    view = pool.layer_view(0)
+    # this rank fills (and later reads) only its own slice of the request
+    n = end - start
+    pos = torch.arange(start, end, device=dev)
+    x = synth.latents(max(n, 1), D, 100 + rank, dev)[:n]
+    pe = synth.normal_bf16((max(n, 1), DR), 200 + rank, dev)[:n]
+    slots = (pt[0, pos // 64].long() * 64 + pos % 64).contiguous()
+    if n > 0:
+        ops.fused_write(x, pe, slots, pool.write_rotation_t(0), pool.codec(0), view,
+                        seq_lens=torch.full((n,), ctx, dtype=torch.int32, device=dev),
+                        req_idx=torch.zeros(n, dtype=torch.int64, device=dev), positions=pos.to(torch.int32))
+    q = synth.normal_bf16((1, HEADS, D + DR), 3, dev)
+    sl = torch.tensor([ctx], dtype=torch.int32, device=dev)
+    rng = torch.tensor([[start, end]], dtype=torch.int32, device=dev)
+    splits = args.splits or ops.default_num_splits(1, max(n, 64))
+    parts = splits + 1
+    part_o = torch.empty(1, HEADS, parts, D, device=dev)
+    part_lse = torch.empty(1, HEADS, parts, device=dev)
+    scratch = torch.empty(1, HEADS, D, dtype=torch.bfloat16, device=dev)
+    o_loc = torch.empty(HEADS, D, device=dev)
+    lse_loc = torch.empty(HEADS, device=dev)
+    sm = 1.0 / math.sqrt(192.0)
+
+    def layer():
+        ops.packed_decode(q, view, pt, sl, sm, splits, part_o, part_lse, scratch, token_range=rng)
+        ops.merge_partials(part_o.view(HEADS, parts, D).transpose(0, 1), part_lse.view(HEADS, parts).t(),
+                           out_f32=o_loc, out_lse=lse_loc)
+
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    kern, coll = [], []
+    for it in range(args.warmup + args.steps):
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        ev[0].record()
+        layer()
+        ev[1].record()
+        if world > 1:
+            gather_merge(o_loc, lse_loc)
+        ev[2].record()
+        torch.cuda.synchronize()
+        if it >= args.warmup:
+            kern.append(ev[0].elapsed_time(ev[1]) * 1e3)
+            coll.append(ev[1].elapsed_time(ev[2]) * 1e3)
+    k_us = sorted(kern)[len(kern) // 2]
+    c_us = sorted(coll)[len(coll) // 2]
+    t = torch.tensor([k_us, c_us, k_us + c_us], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return {"mode": "seqsplit", "n_gpus": world, "batch": 1, "ctx": ctx, "tokens_per_rank": n,
+            "num_splits_per_rank": splits, "us_per_layer": float(t[2]), "kernel_us": float(t[0]),
+            "gather_merge_us": float(t[1]),
+            "note": "median over steps of each rank, max over ranks; kernel = local decode + local merge, "
+                    "gather_merge = NCCL all-gather of the FP32 (o, lse) partials + the merge kernel"}
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--mode", choices=["step", "decode-layer", "writer-layer"], default="step",
-                    help="step: the benchmark; *-layer: one layer, 3 launches (for ncu captures)")
+    ap.add_argument("--mode", choices=["step", "decode-layer", "writer-layer", "seqsplit"], default="step",
+                    help="step: the benchmark; *-layer: one layer, 3 launches (for ncu captures); "
+                         "seqsplit: one 128K-token request split over the ranks (latency per layer)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
@@ -527,6 +599,18 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.mode == "seqsplit":
+        torch.cuda.set_device(local)
+        dev = torch.device("cuda", local)
+        if world > 1:
+            torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        res = run_seqsplit(args, rank, world, dev)
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+        if rank == 0:
+            print(json.dumps(res))
+        return 0
     if args.mode != "step":
         profile_layer(args, args.mode.split("-")[0])
         return 0

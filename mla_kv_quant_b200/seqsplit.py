@@ -36,17 +36,22 @@ def gather_merge(o_local: torch.Tensor, lse_local: torch.Tensor, group=None,
                  merge: Callable[[torch.Tensor, torch.Tensor], tuple[torch.Tensor, torch.Tensor]] | None = None):
     """All-gather per-rank partials ``o [rows, D]`` / ``lse [rows]`` and LSE-merge them.
 
+    One collective: each rank packs its rows as ``[o (D) | lse | pad]`` (D + 4 floats, so
+    rows stay 16-byte aligned) and a single ``all_gather_into_tensor`` moves them; the
+    merge reads strided views of the gathered buffer.
     ``merge(parts_o [world, rows, D], parts_lse [world, rows]) -> (out, lse)``; the
     default is the CUDA merge kernel (``rolaq_merge_partials``) writing FP32.
     """
     world = dist.get_world_size(group)
     rows, d = o_local.shape
-    flat_o = torch.empty(world * rows, d, dtype=o_local.dtype, device=o_local.device)
-    flat_lse = torch.empty(world * rows, dtype=lse_local.dtype, device=lse_local.device)
-    dist.all_gather_into_tensor(flat_o, o_local.contiguous(), group=group)
-    dist.all_gather_into_tensor(flat_lse, lse_local.contiguous(), group=group)
-    parts_o = flat_o.view(world, rows, d)
-    parts_lse = flat_lse.view(world, rows)
+    packed = torch.zeros(rows, d + 4, dtype=torch.float32, device=o_local.device)
+    packed[:, :d] = o_local
+    packed[:, d] = lse_local
+    flat = torch.empty(world * rows, d + 4, dtype=torch.float32, device=o_local.device)
+    dist.all_gather_into_tensor(flat, packed, group=group)
+    parts = flat.view(world, rows, d + 4)
+    parts_o = parts[:, :, :d]
+    parts_lse = parts[:, :, d]
     if merge is not None:
         return merge(parts_o, parts_lse)
     out = torch.empty(rows, d, dtype=torch.float32, device=o_local.device)
