@@ -541,14 +541,12 @@ def run_seqsplit(args, rank, world, dev):
     part_o = torch.empty(1, HEADS, parts, D, device=dev)
     part_lse = torch.empty(1, HEADS, parts, device=dev)
     scratch = torch.empty(1, HEADS, D, dtype=torch.bfloat16, device=dev)
-    o_loc = torch.empty(HEADS, D, device=dev)
     lse_loc = torch.empty(HEADS, device=dev)
+    o_loc = scratch.view(HEADS, D)
     sm = 1.0 / math.sqrt(192.0)
 
-    def layer():
-        ops.packed_decode(q, view, pt, sl, sm, splits, part_o, part_lse, scratch, token_range=rng)
-        ops.merge_partials(part_o.view(HEADS, parts, D).transpose(0, 1), part_lse.view(HEADS, parts).t(),
-                           out_f32=o_loc, out_lse=lse_loc)
+    def layer():  # the slice's merged output (BF16) and LSE, as SequenceSplitDecoder.local_partial
+        ops.packed_decode(q, view, pt, sl, sm, splits, part_o, part_lse, scratch, out_lse=lse_loc, token_range=rng)
 
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     kern, coll = [], []
@@ -574,8 +572,9 @@ def run_seqsplit(args, rank, world, dev):
     return {"mode": "seqsplit", "n_gpus": world, "batch": 1, "ctx": ctx, "tokens_per_rank": n,
             "num_splits_per_rank": splits, "us_per_layer": float(t[2]), "kernel_us": float(t[0]),
             "gather_merge_us": float(t[1]),
-            "note": "median over steps of each rank, max over ranks; kernel = local decode + local merge, "
-                    "gather_merge = NCCL all-gather of the FP32 (o, lse) partials + the merge kernel"}
+            "note": "median over steps of each rank, max over ranks; kernel = the slice's decode call (INT2 "
+                    "splits + window + merge to one BF16 partial and its LSE), gather_merge = one NCCL "
+                    "all-gather of the (o, lse) partials + the merge kernel"}
 
 
 def main():

@@ -2,10 +2,10 @@
 
 Each rank owns one contiguous, page-aligned slice of every request's positions
 (and the cache pages of that slice).  It runs the packed decode kernel restricted
-to its slice (``token_range``), LSE-merges its own splits into one FP32 partial
-``(o, lse)`` per (request, head), and the ranks exchange those partials with one
-NCCL ``all_gather_into_tensor``: ``B * H * (D + 1) * 4`` bytes per rank, about 33 KB
-for one DeepSeek-V2-Lite request.  Every rank then merges the ``world`` partials
+to its slice (``token_range``), which merges its own splits into one partial
+``(o, lse)`` per (request, head) (``o`` rounded to BF16 once, like the final output),
+and the ranks exchange those partials with one NCCL ``all_gather_into_tensor`` of
+``B * H * (D + 4) * 4`` bytes per rank, about 33 KB for one DeepSeek-V2-Lite request.  Every rank then merges the ``world`` partials
 with the same LSE kernel and holds the full output.
 
 The reference serves one GPU only (``deployment/serve.py:135-136``); this module
@@ -34,7 +34,8 @@ def rank_token_range(seq_len: int, world: int, rank: int, page: int = ops.PAGE) 
 
 def gather_merge(o_local: torch.Tensor, lse_local: torch.Tensor, group=None,
                  merge: Callable[[torch.Tensor, torch.Tensor], tuple[torch.Tensor, torch.Tensor]] | None = None):
-    """All-gather per-rank partials ``o [rows, D]`` / ``lse [rows]`` and LSE-merge them.
+    """All-gather per-rank partials ``o [rows, D]`` (FP32 or BF16) / ``lse [rows]`` and
+    LSE-merge them.
 
     One collective: each rank packs its rows as ``[o (D) | lse | pad]`` (D + 4 floats, so
     rows stay 16-byte aligned) and a single ``all_gather_into_tensor`` moves them; the
@@ -45,7 +46,7 @@ def gather_merge(o_local: torch.Tensor, lse_local: torch.Tensor, group=None,
     world = dist.get_world_size(group)
     rows, d = o_local.shape
     packed = torch.zeros(rows, d + 4, dtype=torch.float32, device=o_local.device)
-    packed[:, :d] = o_local
+    packed[:, :d] = o_local  # FP32 or BF16 partials
     packed[:, d] = lse_local
     flat = torch.empty(world * rows, d + 4, dtype=torch.float32, device=o_local.device)
     dist.all_gather_into_tensor(flat, packed, group=group)
@@ -70,19 +71,18 @@ class SequenceSplitDecoder:
         self.rank = dist.get_rank(group)
 
     def local_partial(self, q, layer_id, page_table, seq_lens, sm_scale, num_splits, token_range):
+        """This rank's slice: the decode call's merged output (BF16) and its LSE, per
+        (request, head).  The output is rounded to BF16 once here, as the final output is."""
         b, h, _ = q.shape
         d = self.pool.kv_lora_rank
         parts = num_splits + 1
         part_o = torch.empty(b, h, parts, d, dtype=torch.float32, device=q.device)
         part_lse = torch.empty(b, h, parts, dtype=torch.float32, device=q.device)
-        scratch_out = torch.empty(b, h, d, dtype=torch.bfloat16, device=q.device)
+        o = torch.empty(b, h, d, dtype=torch.bfloat16, device=q.device)
+        lse = torch.empty(b, h, dtype=torch.float32, device=q.device)
         ops.packed_decode(q, self.pool.layer_view(layer_id), page_table, seq_lens, sm_scale, num_splits, part_o,
-                          part_lse, scratch_out, token_range=token_range)
-        o = torch.empty(b * h, d, dtype=torch.float32, device=q.device)
-        lse = torch.empty(b * h, dtype=torch.float32, device=q.device)
-        ops.merge_partials(part_o.view(b * h, parts, d).transpose(0, 1), part_lse.view(b * h, parts).t(),
-                           out_f32=o, out_lse=lse)
-        return o, lse
+                          part_lse, o, out_lse=lse, token_range=token_range)
+        return o.view(b * h, d), lse.view(b * h)
 
     def decode(self, q, layer_id, page_table, seq_lens_host: list[int], seq_lens, sm_scale, num_splits=4):
         """``q [B, H, D + Dr]`` -> ``out [B, H, D]`` BF16 on every rank."""
