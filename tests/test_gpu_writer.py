@@ -139,3 +139,42 @@ def test_fused_write_rejects_bad_arguments():
         ops.fused_write(x[:, :256], pe, torch.arange(4, device="cuda"), rt, ops.codec_serving(0.9, 1.0), pool.view())
     with pytest.raises(_lib.RolaqError, match="finite and > 0"):
         ops.fused_write(x, pe, torch.arange(4, device="cuda"), rt, _lib.Codec(0.0, 1.0, 1.5), pool.view())
+
+
+@pytest.mark.parametrize("side", ["at", "above", "below"])
+@pytest.mark.parametrize("sign", [1, -1])
+def test_fused_write_codes_at_quotient_boundaries(side, sign):
+    """The threshold sits exactly on a normalised value that many elements share (and one
+    FP32 step either side of it).  With the identity rotation the kernel's rotated rows are
+    the BF16 inputs, so these elements are decided by the writer's exact quotient bounds
+    ([n >= t] with n == t must hold, with n one step below t must not)."""
+    d, dr, n = 512, 64, 256
+    rng = np.random.default_rng(11)
+    base = (rng.integers(-3, 4, size=(n, d)) * np.exp2(rng.integers(-3, 4, size=(n, 1)))).astype(np.float32)
+    x = torch.from_numpy(base).to(torch.bfloat16)  # small integers times powers of two: exact
+    g = base.reshape(n, d // 128, 128)
+    mean = ocodec.group_sum(g) * ocodec.INV_GROUP
+    diff = g - mean[..., None]
+    std = np.sqrt(ocodec.group_sum(diff * diff) * ocodec.INV_GROUP + ocodec.EPS)
+    nrm = diff / std[..., None]
+    cand = nrm[(sign * nrm > 0.55) & (sign * nrm < 1.45)]
+    vals, counts = np.unique(cand, return_counts=True)
+    t = np.float32(abs(vals[np.argmax(counts)]))
+    t = {"at": t, "above": np.nextafter(t, np.float32(np.inf)), "below": np.nextafter(t, np.float32(-np.inf))}[side]
+    assert np.sum(np.abs(nrm) == np.float32(abs(vals[np.argmax(counts)]))) >= 8  # the boundary is populated
+
+    num_slots = 64 * (n // 64 + 2)
+    pool = GpuPool(num_slots, d, dr, max_reqs=4)
+    slots = (torch.arange(n) + 64).cuda()
+    rt = torch.eye(d, dtype=torch.bfloat16, device="cuda")
+    codec = ops.codec_serving(float(t), synth.signal_gain(0.85))
+    assert np.float32(codec.threshold) == t
+    pe = synth.normal_bf16((n, dr), seed=1, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ops.fused_write(x.cuda(), pe, slots, rt, codec, pool.view(), err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    oc, osc, oze = ocodec.encode(base, *oracle_scalars(codec))
+    s = slots.cpu().numpy()
+    assert np.array_equal(pool.codes.cpu().numpy()[s], ocodec.pack(oc))
+    assert np.array_equal(pool.params.cpu().numpy()[s], ocodec.params_array(osc, oze))
