@@ -889,28 +889,53 @@ __global__ void __launch_bounds__(128) merge_window_kernel(const DecodeArgs a, i
     qr[3] = __uint_as_float(w.y & 0xFFFF0000u);
   }
   __syncthreads();
-  for (int p = warp; p < nw; p += 4) {  // scores: a warp per row
-    const int64_t slot = rslot[p], r = rrow[p];
-    float acc = 0.f;
-    if (slot >= 0) {
+  // scores: a warp per row, rows p = warp + 4 i; the loads of four rows are issued before
+  // any of them is used (one memory round trip per four rows, not per row)
+  for (int i0 = 0; i0 < kMaxWindow / 4; i0 += 4) {
+    uint2 hv[4][4], rv[4];
+    bool ring[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        float v[4];
-        window_elems4<D, DR>(a, slot, r, 4 * lane + 128 * u, v);
+    for (int ii = 0; ii < 4; ++ii) {
+      const int p = warp + 4 * (i0 + ii);
+      const int64_t slot = p < nw ? rslot[p] : -1, r = p < nw ? rrow[p] : -1;
+      ring[ii] = slot >= 0 && r >= 0;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) acc = fmaf(qv[4 * u + c], v[c], acc);
-      }
-      if (lane < DR / 4) {
-        const uint2 w = *reinterpret_cast<const uint2*>(a.cache.rope + slot * DR + 4 * lane);
-        acc = fmaf(qr[0], __uint_as_float(w.x << 16), acc);
-        acc = fmaf(qr[1], __uint_as_float(w.x & 0xFFFF0000u), acc);
-        acc = fmaf(qr[2], __uint_as_float(w.y << 16), acc);
-        acc = fmaf(qr[3], __uint_as_float(w.y & 0xFFFF0000u), acc);
-      }
+      for (int u = 0; u < 4; ++u)
+        hv[ii][u] = ring[ii] ? *reinterpret_cast<const uint2*>(a.cache.hp + r * D + 4 * lane + 128 * u)
+                             : make_uint2(0, 0);
+      rv[ii] = (slot >= 0 && lane < DR / 4) ? *reinterpret_cast<const uint2*>(a.cache.rope + slot * DR + 4 * lane)
+                                           : make_uint2(0, 0);
     }
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
-    if (lane == 0) sc[p] = acc * a.sm_scale;
+    for (int ii = 0; ii < 4; ++ii) {
+      const int p = warp + 4 * (i0 + ii);
+      if (p >= nw) break;  // uniform across the warp
+      const int64_t slot = rslot[p];
+      float acc = 0.f;
+      if (slot >= 0) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          float v[4];
+          if (ring[ii]) {
+            v[0] = __uint_as_float(hv[ii][u].x << 16);
+            v[1] = __uint_as_float(hv[ii][u].x & 0xFFFF0000u);
+            v[2] = __uint_as_float(hv[ii][u].y << 16);
+            v[3] = __uint_as_float(hv[ii][u].y & 0xFFFF0000u);
+          } else {  // the ring row no longer belongs to the slot: INT2 codes
+            window_elems4<D, DR>(a, slot, -1, 4 * lane + 128 * u, v);
+          }
+#pragma unroll
+          for (int c = 0; c < 4; ++c) acc = fmaf(qv[4 * u + c], v[c], acc);
+        }
+        acc = fmaf(qr[0], __uint_as_float(rv[ii].x << 16), acc);
+        acc = fmaf(qr[1], __uint_as_float(rv[ii].x & 0xFFFF0000u), acc);
+        acc = fmaf(qr[2], __uint_as_float(rv[ii].y << 16), acc);
+        acc = fmaf(qr[3], __uint_as_float(rv[ii].y & 0xFFFF0000u), acc);
+      }
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+      if (lane == 0) sc[p] = acc * a.sm_scale;
+    }
   }
   __syncthreads();
   const float* lse_row = a.part_lse + static_cast<int64_t>(row) * S;
@@ -943,14 +968,24 @@ __global__ void __launch_bounds__(128) merge_window_kernel(const DecodeArgs a, i
   // window partial of this thread's 4 elements (rows re-read: L1 hits)
   const int j = 4 * tid;
   float ow[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int p = 0; p < nw; ++p) {
-    const int64_t slot = rslot[p];
-    if (slot < 0) continue;
-    float v[4];
-    window_elems4<D, DR>(a, slot, rrow[p], j, v);
-    const float e = sc[p];
+  for (int p0 = 0; p0 < nw; p0 += 4) {  // four rows' loads in flight at once
+    float v[4][4];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) ow[c] = fmaf(e, v[c], ow[c]);
+    for (int u = 0; u < 4; ++u) {
+      const int p = p0 + u;
+      const int64_t slot = p < nw ? rslot[p] : -1;
+      if (slot >= 0) {
+        window_elems4<D, DR>(a, slot, rrow[p], j, v[u]);
+      } else {
+        v[u][0] = v[u][1] = v[u][2] = v[u][3] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float e = p0 + u < nw ? sc[p0 + u] : 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) ow[c] = fmaf(e, v[u][c], ow[c]);
+    }
   }
   __syncthreads();
   float den = 0.f;  // every thread sums the same weights in the same order
