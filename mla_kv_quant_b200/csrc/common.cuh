@@ -284,6 +284,14 @@ __device__ __forceinline__ uint32_t half2_to_e4m3x2(__half2 h) {
       __nv_cvt_halfraw2_to_fp8x2(static_cast<__half2_raw>(h), __NV_SATFINITE, __NV_E4M3));
 }
 
+// Programmatic dependent launch: a kernel launched with the programmatic stream
+// serialization attribute may start once every CTA of the kernel before it in the stream
+// has executed launch_dependents (or exited); griddepcontrol.wait then blocks until that
+// grid has completed and its memory operations are visible.  Without such a launch the
+// wait returns at once.
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }

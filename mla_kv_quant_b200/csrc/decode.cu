@@ -805,13 +805,19 @@ __global__ void merge_kernel(const float* __restrict__ part_o, int64_t row_strid
   if (threadIdx.x == 0 && out_lse) out_lse[row] = den > 0.f ? mref + logf(den) : -INFINITY;
 }
 
-// Window split + LSE merge for the tcgen05 path, one CTA per (request, head) and no
-// shared-memory copy of the rows (so that every CTA of a launch is resident at once): a
-// warp per window row computes the score (lane l owns elements 4l + 128u + c and the rope
-// elements 4l + c), warp 0 the softmax, then each thread re-reads its 4 elements of every
-// row (L1-resident by then) for the window partial and merges it with the num_splits INT2
-// partials the tcgen05 kernel wrote.  The window partial is also stored in split
-// num_splits of part_o / part_lse, so the scratch holds every partial after the call.
+// Window split + LSE merge for the tcgen05 path, one CTA per (request, 4 heads), 256 threads.
+//
+// Phase 1 does not read the INT2 partials, so it runs while the tcgen05 kernel drains (this
+// kernel is launched as its programmatic dependent): the window rows' slots and ring rows
+// once per CTA; scores with a warp pair per head (warp 2h + e takes rows e, e + 2, ..; lane l
+// owns latent elements 4l + 128u + c and rope elements 4l + c); the window softmax (a warp
+// per head); the window partial (thread: head tid / 64, elements 8 (tid % 64) ..+8), stored
+// as split num_splits of part_o / part_lse so that the scratch holds every partial after the
+// call.  Phase 2, after griddepcontrol.wait: each warp reads its head's split LSEs (lane =
+// split; the weights reach the other lanes by shuffle) and merges the partials.
+constexpr int kMwHeads = 4;
+constexpr int kMwThreads = 256;
+
 template <int D, int DR>
 __device__ __forceinline__ void window_elems4(const DecodeArgs& a, int64_t slot, int64_t r, int e0, float (&v)[4]) {
   if (r >= 0) {
@@ -828,15 +834,37 @@ __device__ __forceinline__ void window_elems4(const DecodeArgs& a, int64_t slot,
   }
 }
 
+// Elements e0 .. e0 + 7 of a window row: the BF16 ring row r, or (r < 0: the ring row no
+// longer belongs to the slot) the slot's INT2 codes dequantised as (code - zero) * scale.
 template <int D, int DR>
-__global__ void __launch_bounds__(128) merge_window_kernel(const DecodeArgs a, int heads, uint16_t* __restrict__ out,
-                                                           int64_t out_sb, int64_t out_sh, float* __restrict__ out_lse) {
-  static_assert(D == 4 * 128 && DR == 64, "four latent elements per thread, 16 rope lanes");
-  extern __shared__ float wts[];  // [num_splits]
-  __shared__ float sc[kMaxWindow];
+__device__ __forceinline__ void window_elems8(const DecodeArgs& a, int64_t slot, int64_t r, int e0, float (&v)[8]) {
+  if (r >= 0) {
+    const uint4 w = *reinterpret_cast<const uint4*>(a.cache.hp + r * D + e0);
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      v[2 * c] = __uint_as_float(ws[c] << 16);
+      v[2 * c + 1] = __uint_as_float(ws[c] & 0xFFFF0000u);
+    }
+  } else {
+    const uint32_t cb = *reinterpret_cast<const uint16_t*>(a.cache.codes + slot * (D / 4) + e0 / 4);
+    const float2 sz = reinterpret_cast<const float2*>(a.cache.params)[slot * (D / 128) + e0 / 128];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) v[c] = __fmul_rn(__fsub_rn(static_cast<float>((cb >> (2 * c)) & 3u), sz.y), sz.x);
+  }
+}
+
+template <int D, int DR>
+__global__ void __launch_bounds__(kMwThreads) merge_window_kernel(const DecodeArgs a, int heads,
+                                                                  uint16_t* __restrict__ out, int64_t out_sb,
+                                                                  int64_t out_sh, float* __restrict__ out_lse) {
+  static_assert(D == 4 * 128 && DR == 64, "four latent elements per lane, 16 rope lanes; 8 elements per thread");
+  static_assert(kMwThreads == kMwHeads * (D / 8) && kMwThreads == 64 * kMwHeads, "thread <-> (head, elements)");
+  __shared__ float sc[kMwHeads][kMaxWindow];
   __shared__ int64_t rslot[kMaxWindow], rrow[kMaxWindow];
-  __shared__ float stat[4];
-  const int row = blockIdx.x, b = row / heads, h = row % heads;
+  __shared__ float stat[kMwHeads][2];  // window lse, window sum of exp
+  const int hgroups = heads / kMwHeads;
+  const int b = blockIdx.x / hgroups, h0 = (blockIdx.x % hgroups) * kMwHeads;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int S = a.num_splits + 1;
   int L = a.seq_lens[b];
@@ -854,8 +882,6 @@ __global__ void __launch_bounds__(128) merge_window_kernel(const DecodeArgs a, i
   const int s2 = min(max(rs, hs), L), e2 = max(min(re, L), s2);
   const int n1 = e1 - s1;
   const int nw = n1 + (e2 - s2);  // <= sink + recent <= kMaxWindow (checked by the host)
-  if (tid == 32)  // the INT2 partials of this row are read last: start them towards L2 now
-    prefetch_l2(a.part_o + static_cast<int64_t>(row) * S * D, static_cast<uint32_t>(a.num_splits * D * 4));
   if (tid < nw) {
     const int pos = tid < n1 ? s1 + tid : s2 + (tid - n1);
     const int64_t page = a.page_table[b * a.pt_stride + pos / kPage];
@@ -870,8 +896,9 @@ __global__ void __launch_bounds__(128) merge_window_kernel(const DecodeArgs a, i
     rslot[tid] = slot;
     rrow[tid] = r;
   }
-  // this head's query at the lane's elements
-  const uint16_t* qh = a.q + b * a.q_sb + h * a.q_sh;
+  // the query of head h0 + hw at the lane's elements
+  const int hw = warp >> 1, par = warp & 1;
+  const uint16_t* qh = a.q + b * a.q_sb + (h0 + hw) * a.q_sh;
   float qv[16], qr[4];
 #pragma unroll
   for (int u = 0; u < 4; ++u) {
@@ -889,14 +916,13 @@ __global__ void __launch_bounds__(128) merge_window_kernel(const DecodeArgs a, i
     qr[3] = __uint_as_float(w.y & 0xFFFF0000u);
   }
   __syncthreads();
-  // scores: a warp per row, rows p = warp + 4 i; the loads of four rows are issued before
-  // any of them is used (one memory round trip per four rows, not per row)
-  for (int i0 = 0; i0 < kMaxWindow / 4; i0 += 4) {
+  // scores: rows p = par + 2 i; the loads of four rows are issued before any of them is used
+  for (int i0 = 0; i0 < kMaxWindow / 2 && par + 2 * i0 < nw; i0 += 4) {
     uint2 hv[4][4], rv[4];
     bool ring[4];
 #pragma unroll
     for (int ii = 0; ii < 4; ++ii) {
-      const int p = warp + 4 * (i0 + ii);
+      const int p = par + 2 * (i0 + ii);
       const int64_t slot = p < nw ? rslot[p] : -1, r = p < nw ? rrow[p] : -1;
       ring[ii] = slot >= 0 && r >= 0;
 #pragma unroll
@@ -908,7 +934,7 @@ __global__ void __launch_bounds__(128) merge_window_kernel(const DecodeArgs a, i
     }
 #pragma unroll
     for (int ii = 0; ii < 4; ++ii) {
-      const int p = warp + 4 * (i0 + ii);
+      const int p = par + 2 * (i0 + ii);
       if (p >= nw) break;  // uniform across the warp
       const int64_t slot = rslot[p];
       float acc = 0.f;
@@ -934,13 +960,12 @@ __global__ void __launch_bounds__(128) merge_window_kernel(const DecodeArgs a, i
       }
 #pragma unroll
       for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
-      if (lane == 0) sc[p] = acc * a.sm_scale;
+      if (lane == 0) sc[hw][p] = acc * a.sm_scale;
     }
   }
   __syncthreads();
-  const float* lse_row = a.part_lse + static_cast<int64_t>(row) * S;
-  if (warp == 0) {  // window softmax
-    const float x = lane < nw ? sc[lane] : -INFINITY;
+  if (warp < kMwHeads) {  // window softmax of head h0 + warp
+    const float x = lane < nw ? sc[warp][lane] : -INFINITY;
     float m = x;
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
@@ -948,71 +973,103 @@ __global__ void __launch_bounds__(128) merge_window_kernel(const DecodeArgs a, i
     float l = e;
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
-    if (lane < nw) sc[lane] = e;
+    if (lane < nw) sc[warp][lane] = e;
     if (lane == 0) {
-      stat[0] = nw > 0 ? m + logf(l) : -INFINITY;  // window lse
-      stat[1] = l;
+      stat[warp][0] = nw > 0 ? m + logf(l) : -INFINITY;
+      stat[warp][1] = l;
     }
-  } else if (warp == 1) {  // max of the INT2 partials' lse
-    float m = -INFINITY;
-    for (int p = lane; p < a.num_splits; p += 32) m = fmaxf(m, lse_row[p]);
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
-    if (lane == 0) stat[2] = m;
   }
   __syncthreads();
-  const float lse_w = stat[0], lw = stat[1];
-  const float mref0 = fmaxf(stat[2], lse_w);
-  const float mref = mref0 == -INFINITY ? 0.f : mref0;
-  for (int p = tid; p < a.num_splits; p += blockDim.x) wts[p] = __expf(lse_row[p] - mref);
-  // window partial of this thread's 4 elements (rows re-read: L1 hits)
-  const int j = 4 * tid;
-  float ow[4] = {0.f, 0.f, 0.f, 0.f};
+  // window partial of head hh at elements j .. j + 7 (rows re-read: L1 hits)
+  const int hh = tid >> 6, j = 8 * (tid & 63);
+  float ow[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) ow[c] = 0.f;
   for (int p0 = 0; p0 < nw; p0 += 4) {  // four rows' loads in flight at once
-    float v[4][4];
+    float v[4][8];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int p = p0 + u;
       const int64_t slot = p < nw ? rslot[p] : -1;
       if (slot >= 0) {
-        window_elems4<D, DR>(a, slot, rrow[p], j, v[u]);
+        window_elems8<D, DR>(a, slot, rrow[p], j, v[u]);
       } else {
-        v[u][0] = v[u][1] = v[u][2] = v[u][3] = 0.f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) v[u][c] = 0.f;
       }
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      const float e = p0 + u < nw ? sc[p0 + u] : 0.f;
+      const float e = p0 + u < nw ? sc[hh][p0 + u] : 0.f;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) ow[c] = fmaf(e, v[u][c], ow[c]);
+      for (int c = 0; c < 8; ++c) ow[c] = fmaf(e, v[u][c], ow[c]);
     }
   }
-  __syncthreads();
-  float den = 0.f;  // every thread sums the same weights in the same order
-  for (int p = 0; p < a.num_splits; ++p) den += wts[p];
+  const float lse_w = stat[hh][0];
+  const float il = nw > 0 ? 1.f / stat[hh][1] : 0.f;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) ow[c] *= il;
+  const int64_t row = static_cast<int64_t>(b) * heads + h0 + hh;
+  float* prow = a.part_o + row * S * D;
+  {
+    float4* dst = reinterpret_cast<float4*>(prow + static_cast<int64_t>(a.num_splits) * D + j);
+    dst[0] = make_float4(ow[0], ow[1], ow[2], ow[3]);
+    dst[1] = make_float4(ow[4], ow[5], ow[6], ow[7]);
+  }
+  if ((tid & 63) == 0) a.part_lse[row * S + a.num_splits] = lse_w;
+
+  // ---- phase 2: the INT2 partials, written by the kernel this launch depends on ----
+  grid_dependency_wait();
+  const int ns = a.num_splits;
+  const float* lse_row = a.part_lse + row * S;
+  float m = lse_w;
+  for (int p = lane; p < ns; p += 32) m = fmaxf(m, lse_row[p]);
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+  const float mref = m == -INFINITY ? 0.f : m;
   const float ww = lse_w == -INFINITY ? 0.f : __expf(lse_w - mref);
+  float acc[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) acc[c] = ww * ow[c];
+  float den = 0.f;
+  for (int pb = 0; pb < ns; pb += 32) {
+    const int cnt = min(32, ns - pb);
+    const float wl = lane < cnt ? __expf(lse_row[pb + lane] - mref) : 0.f;  // weight of split pb + lane
+    den += wl;
+    for (int q = 0; q < cnt; q += 4) {  // four splits' loads in flight at once
+      float4 v[4][2];
+      float w[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        w[u] = __shfl_sync(0xFFFFFFFFu, wl, (q + u) & 31);
+        if (q + u >= cnt) w[u] = 0.f;
+        const float4* src =
+            reinterpret_cast<const float4*>(prow + static_cast<int64_t>(pb + min(q + u, cnt - 1)) * D + j);
+        v[u][0] = src[0];
+        v[u][1] = src[1];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {  // empty splits (weight 0) are masked, not multiplied
+        const float vv[8] = {v[u][0].x, v[u][0].y, v[u][0].z, v[u][0].w, v[u][1].x, v[u][1].y, v[u][1].z, v[u][1].w};
+#pragma unroll
+        for (int c = 0; c < 8; ++c) acc[c] = w[u] > 0.f ? fmaf(w[u], vv[c], acc[c]) : acc[c];
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) den += __shfl_xor_sync(0xFFFFFFFFu, den, o);
   den += ww;
   const float inv = den > 0.f ? 1.f / den : 0.f;
-  const float il = nw > 0 ? 1.f / lw : 0.f;
-  const float4 o4 = make_float4(ow[0] * il, ow[1] * il, ow[2] * il, ow[3] * il);
-  float* prow = a.part_o + static_cast<int64_t>(row) * S * D;
-  *reinterpret_cast<float4*>(prow + static_cast<int64_t>(a.num_splits) * D + j) = o4;
-  if (tid == 0) a.part_lse[static_cast<int64_t>(row) * S + a.num_splits] = lse_w;
-  float4 acc = make_float4(ww * o4.x, ww * o4.y, ww * o4.z, ww * o4.w);
-#pragma unroll 4
-  for (int p = 0; p < a.num_splits; ++p) {
-    const float w = wts[p];
-    const float4 v = *reinterpret_cast<const float4*>(prow + static_cast<int64_t>(p) * D + j);
-    acc.x = w > 0.f ? fmaf(w, v.x, acc.x) : acc.x;
-    acc.y = w > 0.f ? fmaf(w, v.y, acc.y) : acc.y;
-    acc.z = w > 0.f ? fmaf(w, v.z, acc.z) : acc.z;
-    acc.w = w > 0.f ? fmaf(w, v.w, acc.w) : acc.w;
+  uint32_t pk[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const __nv_bfloat162 v2 = __floats2bfloat162_rn(acc[2 * c] * inv, acc[2 * c + 1] * inv);
+    pk[c] = *reinterpret_cast<const uint32_t*>(&v2);
   }
-  const __nv_bfloat162 o01 = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
-  const __nv_bfloat162 o23 = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
-  *reinterpret_cast<uint2*>(out + b * out_sb + h * out_sh + j) =
-      make_uint2(*reinterpret_cast<const uint32_t*>(&o01), *reinterpret_cast<const uint32_t*>(&o23));
-  if (tid == 0 && out_lse) out_lse[row] = den > 0.f ? mref + logf(den) : -INFINITY;
+  uint2* o2 = reinterpret_cast<uint2*>(out + b * out_sb + (h0 + hh) * out_sh + j);  // 8-byte aligned rows
+  o2[0] = make_uint2(pk[0], pk[1]);
+  o2[1] = make_uint2(pk[2], pk[3]);
+  if ((tid & 63) == 0 && out_lse) out_lse[row] = den > 0.f ? mref + logf(den) : -INFINITY;
 }
 
 // ---- host side ---------------------------------------------------------------------------
@@ -1109,12 +1166,23 @@ int launch_decode_merged(const DecodeArgs& a, int heads, uint16_t* out, int64_t 
   if ((reinterpret_cast<uintptr_t>(out) & 7u) || (out_sb & 3) || (out_sh & 3) ||
       (reinterpret_cast<uintptr_t>(a.part_o) & 15u))
     return ROLAQ_EUNSUPPORTED;
-  const size_t smem = size_t(a.num_splits) * sizeof(float);
-  if (smem > 48 * 1024) return ROLAQ_EUNSUPPORTED;
+  if (heads % kMwHeads != 0) return ROLAQ_EUNSUPPORTED;
   int rc = launch_decode_tc(a, s);
   if (rc != ROLAQ_OK) return rc;
-  merge_window_kernel<512, 64><<<static_cast<unsigned>(int64_t(a.batch) * heads), 128, smem, s>>>(
-      a, heads, out, out_sb, out_sh, out_lse);
+  // Programmatic dependent launch: the window phase overlaps the tcgen05 kernel's last CTAs;
+  // the merge waits for that grid's completion (griddepcontrol.wait) before reading partials.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(int64_t(a.batch) * heads / kMwHeads));
+  cfg.blockDim = dim3(kMwThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, merge_window_kernel<512, 64>, a, heads, out, out_sb, out_sh, out_lse) != cudaSuccess)
+    return ROLAQ_ECUDA;
   return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;
 }
 

@@ -24,7 +24,8 @@
 //     query, exact for BF16 after a per-head power-of-two scale), + the rope part in
 //     kind::f16 with k_pe staged by TMA;
 //   * the token threads turn scores into P = 2^(s - m_ref) against a reference max that
-//     moves only when a tile max exceeds it by more than kTau (lazy rescaling), and
+//     moves only when a tile max exceeds it by more than kTau (lazy rescaling; the tile
+//     maxima are exchanged among the four warps of a head set, 128 threads), and
 //     write P' = P s_g E_g (E_g a per-group power of two that moves only when the group
 //     scale outgrows it) as two E4M3 terms;
 //   * PV = kind::f8f6f4 (M = 128 latent elements of a group, N = 32, K = 128 tokens)
@@ -73,8 +74,9 @@ constexpr int OFF_F = OFF_PAR + 2 * PAR_STAGE;
 constexpr int F_QSUM = 0;               // [NG][H]     sum of the query over the group
 constexpr int F_KINV = F_QSUM + NG * H;  // [H]         2^(9 - k_h)
 constexpr int F_HMAX = F_KINV + H;       // [2][H][4]   tile max per head and token quarter
-constexpr int F_GMAX = F_HMAX + 2 * H * 4;   // [2][NG][4]  tile max of s_g per token quarter
-constexpr int F_FINL = F_GMAX + 2 * NG * 4;  // [4][H]      sum P per token quarter
+constexpr int F_GMAX = F_HMAX + 2 * H * 4;        // [2][NG][NG][4] tile max of s_g per head set,
+                                                  //                group and token quarter
+constexpr int F_FINL = F_GMAX + 2 * NG * NG * 4;  // [4][H]      sum P per token quarter
 constexpr int F_FINY = F_FINL + 4 * H;       // [4][NG][H]  sum P' z per token quarter
 constexpr int F_TOTAL = F_FINY + 4 * NG * H;
 constexpr int OFF_BAR = OFF_F + ((F_TOTAL * 4 + 15) / 16) * 16;
@@ -136,6 +138,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int b = blockIdx.y, split = blockIdx.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // the window/merge kernel that follows may start its window phase on SMs this grid frees
+  if (tid == 0) grid_launch_dependents();
   const int S = a.num_splits + 1;  // the window split (index num_splits) is written by window_kernel
   int L = a.seq_lens[b];
   if (L < 0) L = 0;
@@ -418,7 +422,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       float s2[4];
       {
-        float A[4] = {0.f, 0.f, 0.f, 0.f}, B[4] = {0.f, 0.f, 0.f, 0.f};
+        // A = sum_g s_g q_g.c and B = -sum_g s_g z_g sum(q_g) for heads (4k + 2jp, +1), a pair
+        // per FFMA2 (the packed FP32 pipe: two IEEE round-to-nearest FMAs per instruction)
+        float2 A[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        float2 B[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
         uint32_t pe[4];
 #pragma unroll
         for (int g2 = 0; g2 < NG; g2 += 2) {  // two groups per TMEM round trip (register budget)
@@ -434,21 +441,27 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int gg = 0; gg < 2; ++gg) {
             const int g = g2 + gg;
             const float4 qs4 = *reinterpret_cast<const float4*>(F + F_QSUM + g * H + 4 * k);
-            const float qs[4] = {qs4.x, qs4.y, qs4.z, qs4.w};
-            const float scz = sc[g] * zz[g];
+            const float2 qs[2] = {make_float2(qs4.x, qs4.y), make_float2(qs4.z, qs4.w)};
+            const float nscz = -sc[g] * zz[g];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float qc = fmaf(__uint_as_float(dq[gg][4 + j]), 0.0625f, __uint_as_float(dq[gg][j]));
-              A[j] = fmaf(sc[g], qc, A[j]);
-              B[j] = fmaf(scz, qs[j], B[j]);
+            for (int jp = 0; jp < 2; ++jp) {
+              const uint32_t* d = dq[gg];  // hi terms d[0..3], lo terms d[4..7] (heads 4k..4k+3)
+              const float2 qc =
+                  make_float2(fmaf(__uint_as_float(d[4 + 2 * jp]), 0.0625f, __uint_as_float(d[2 * jp])),
+                              fmaf(__uint_as_float(d[5 + 2 * jp]), 0.0625f, __uint_as_float(d[2 * jp + 1])));
+              A[jp] = __ffma2_rn(make_float2(sc[g], sc[g]), qc, A[jp]);
+              B[jp] = __ffma2_rn(make_float2(nscz, nscz), qs[jp], B[jp]);
             }
           }
         }
         const float4 ki = *reinterpret_cast<const float4*>(F + F_KINV + 4 * k);
-        const float kinv[4] = {ki.x, ki.y, ki.z, ki.w};
+        const float2 kinv[2] = {make_float2(ki.x, ki.y), make_float2(ki.z, ki.w)};
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          s2[j] = ok ? fmaf(A[j], kinv[j], __uint_as_float(pe[j]) - B[j]) * sl2 : -INFINITY;
+        for (int j = 0; j < 4; ++j) {
+          const float Aj = (j & 1) ? A[j >> 1].y : A[j >> 1].x, Bj = (j & 1) ? B[j >> 1].y : B[j >> 1].x;
+          const float kj = (j & 1) ? kinv[j >> 1].y : kinv[j >> 1].x;
+          s2[j] = ok ? fmaf(Aj, kj, __uint_as_float(pe[j]) + Bj) * sl2 : -INFINITY;
+        }
       }
       mbar_arrive(&bars[B_PFREE + s]);  // params stage s has been read (sc, zz are in registers)
       // -- 1b. codes of tile i+1 into TMEM (QK^T(i) has completed) --
@@ -474,7 +487,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_before();
       }
       // -- 2. tile max per head (lane holds head 4k + 2*b4 + b3 after the exchange) and
-      //       per-quarter max of this thread's group scale --
+      //       per-quarter max of the four group scales --
       {
         const bool u16 = (lane & 16) != 0, u8 = (lane & 8) != 0;
         const float b0 = fmaxf(u16 ? s2[2] : s2[0], __shfl_xor_sync(0xFFFFFFFFu, u16 ? s2[0] : s2[2], 16));
@@ -484,12 +497,19 @@ __global__ void __launch_bounds__(THREADS, 1)
         c = fmaxf(c, __shfl_xor_sync(0xFFFFFFFFu, c, 2));
         c = fmaxf(c, __shfl_xor_sync(0xFFFFFFFFu, c, 1));
         if ((lane & 7) == 0) F[F_HMAX + s * H * 4 + (4 * k + (lane >> 3)) * 4 + q4] = c;
-        float gm = sc[k];
-#pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) gm = fmaxf(gm, __shfl_xor_sync(0xFFFFFFFFu, gm, o));
-        if (lane == 0) F[F_GMAX + s * NG * 4 + k * 4 + q4] = gm;
+        // the four group scales, exchanged the same way (lane then holds group lane >> 3)
+        const float e0 = fmaxf(u16 ? sc[2] : sc[0], __shfl_xor_sync(0xFFFFFFFFu, u16 ? sc[0] : sc[2], 16));
+        const float e1 = fmaxf(u16 ? sc[3] : sc[1], __shfl_xor_sync(0xFFFFFFFFu, u16 ? sc[1] : sc[3], 16));
+        float e = fmaxf(u8 ? e1 : e0, __shfl_xor_sync(0xFFFFFFFFu, u8 ? e0 : e1, 8));
+        e = fmaxf(e, __shfl_xor_sync(0xFFFFFFFFu, e, 4));
+        e = fmaxf(e, __shfl_xor_sync(0xFFFFFFFFu, e, 2));
+        e = fmaxf(e, __shfl_xor_sync(0xFFFFFFFFu, e, 1));
+        if ((lane & 7) == 0) F[F_GMAX + ((s * NG + k) * NG + (lane >> 3)) * 4 + q4] = e;
       }
-      named_bar_sync(1, TOK_THREADS);
+      // The four warps of head set k (one per token quarter) exchange their maxima; the head
+      // sets do not wait for one another.  Each set's group-scale maxima cover all 128 tokens,
+      // so every set takes the same E_g decisions.
+      named_bar_sync(4 + k, 128);
       // -- 3. softmax against the reference max, P' = P s_g E_g as hi + lo / 16 (two E4M3
       //       terms; the residual is scaled by 16 to stay in E4M3's normal range) --
       float alpha[4], gf[NG], mt[4], gm[NG];
@@ -497,7 +517,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int j = 0; j < 4; ++j)  // all table reads first: one shared-memory round trip
         mt[j] = max4(*reinterpret_cast<const float4*>(F + F_HMAX + s * H * 4 + (4 * k + j) * 4));
 #pragma unroll
-      for (int g = 0; g < NG; ++g) gm[g] = max4(*reinterpret_cast<const float4*>(F + F_GMAX + s * NG * 4 + g * 4));
+      for (int g = 0; g < NG; ++g)
+        gm[g] = max4(*reinterpret_cast<const float4*>(F + F_GMAX + ((s * NG + k) * NG + g) * 4));
       bool resc = false;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
