@@ -289,8 +289,17 @@ __device__ __forceinline__ uint32_t half2_to_e4m3x2(__half2 h) {
 // has executed launch_dependents (or exited); griddepcontrol.wait then blocks until that
 // grid has completed and its memory operations are visible.  Without such a launch the
 // wait returns at once.
-__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Maximum of v over the 32 lanes of a full warp (one instruction on sm_100a).
+__device__ __forceinline__ float warp_max_f32(float v) {
+  float r;
+  asm("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
+}
 
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

@@ -73,9 +73,9 @@ constexpr int OFF_F = OFF_PAR + 2 * PAR_STAGE;
 // float scratch
 constexpr int F_QSUM = 0;               // [NG][H]     sum of the query over the group
 constexpr int F_KINV = F_QSUM + NG * H;  // [H]         2^(9 - k_h)
-constexpr int F_HMAX = F_KINV + H;       // [2][H][4]   tile max per head and token quarter
-constexpr int F_GMAX = F_HMAX + 2 * H * 4;        // [2][NG][NG][4] tile max of s_g per head set,
-                                                  //                group and token quarter
+constexpr int F_HMAX = F_KINV + H;       // [2][NG][4][4] tile max per head set, token quarter, head
+constexpr int F_GMAX = F_HMAX + 2 * H * 4;        // [2][NG][4][NG] tile max of s_g per head set,
+                                                  //                token quarter and group
 constexpr int F_FINL = F_GMAX + 2 * NG * NG * 4;  // [4][H]      sum P per token quarter
 constexpr int F_FINY = F_FINL + 4 * H;       // [4][NG][H]  sum P' z per token quarter
 constexpr int F_TOTAL = F_FINY + 4 * NG * H;
@@ -335,16 +335,15 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int t = 32 * q4 + lane;  // token of the tile (TMEM lane)
     const uint32_t lane_base = static_cast<uint32_t>(32 * q4) << 16;
     const float sl2 = a.sm_scale * kLog2e;
-    float m_ref[4], lsum[4], y[NG][4], E[NG];
+    // st: lane d = lane & 7 keeps m_ref of head 4k + d (d < 4) or E of group d - 4 (d >= 4)
+    float st = (lane & 7) < 4 ? -INFINITY : 0.f;
+    float lsum[4], y[NG][4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      m_ref[j] = -INFINITY;
       lsum[j] = 0.f;
 #pragma unroll
       for (int g = 0; g < NG; ++g) y[g][j] = 0.f;
     }
-#pragma unroll
-    for (int g = 0; g < NG; ++g) E[g] = 0.f;
 
     // next tile's codes of group k (32 B)
     uint4 cw0, cw1;
@@ -486,60 +485,62 @@ __global__ void __launch_bounds__(THREADS, 1)
       } else {
         tc_fence_before();
       }
-      // -- 2. tile max per head (lane holds head 4k + 2*b4 + b3 after the exchange) and
-      //       per-quarter max of the four group scales --
+      // -- 2. the warp's tile maxima (its 32 tokens) of the four heads' scores and of the four
+      //       group scales, one redux each, into the head set's table --
       {
-        const bool u16 = (lane & 16) != 0, u8 = (lane & 8) != 0;
-        const float b0 = fmaxf(u16 ? s2[2] : s2[0], __shfl_xor_sync(0xFFFFFFFFu, u16 ? s2[0] : s2[2], 16));
-        const float b1 = fmaxf(u16 ? s2[3] : s2[1], __shfl_xor_sync(0xFFFFFFFFu, u16 ? s2[1] : s2[3], 16));
-        float c = fmaxf(u8 ? b1 : b0, __shfl_xor_sync(0xFFFFFFFFu, u8 ? b0 : b1, 8));
-        c = fmaxf(c, __shfl_xor_sync(0xFFFFFFFFu, c, 4));
-        c = fmaxf(c, __shfl_xor_sync(0xFFFFFFFFu, c, 2));
-        c = fmaxf(c, __shfl_xor_sync(0xFFFFFFFFu, c, 1));
-        if ((lane & 7) == 0) F[F_HMAX + s * H * 4 + (4 * k + (lane >> 3)) * 4 + q4] = c;
-        // the four group scales, exchanged the same way (lane then holds group lane >> 3)
-        const float e0 = fmaxf(u16 ? sc[2] : sc[0], __shfl_xor_sync(0xFFFFFFFFu, u16 ? sc[0] : sc[2], 16));
-        const float e1 = fmaxf(u16 ? sc[3] : sc[1], __shfl_xor_sync(0xFFFFFFFFu, u16 ? sc[1] : sc[3], 16));
-        float e = fmaxf(u8 ? e1 : e0, __shfl_xor_sync(0xFFFFFFFFu, u8 ? e0 : e1, 8));
-        e = fmaxf(e, __shfl_xor_sync(0xFFFFFFFFu, e, 4));
-        e = fmaxf(e, __shfl_xor_sync(0xFFFFFFFFu, e, 2));
-        e = fmaxf(e, __shfl_xor_sync(0xFFFFFFFFu, e, 1));
-        if ((lane & 7) == 0) F[F_GMAX + ((s * NG + k) * NG + (lane >> 3)) * 4 + q4] = e;
+        float hm[4], gx[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) hm[j] = warp_max_f32(s2[j]);
+#pragma unroll
+        for (int g = 0; g < NG; ++g) gx[g] = warp_max_f32(sc[g]);
+        if (lane == 0) {
+          const int row = ((s * NG + k) * 4 + q4) * 4;
+          *reinterpret_cast<float4*>(F + F_HMAX + row) = make_float4(hm[0], hm[1], hm[2], hm[3]);
+          *reinterpret_cast<float4*>(F + F_GMAX + row) = make_float4(gx[0], gx[1], gx[2], gx[3]);
+        }
       }
       // The four warps of head set k (one per token quarter) exchange their maxima; the head
       // sets do not wait for one another.  Each set's group-scale maxima cover all 128 tokens,
       // so every set takes the same E_g decisions.
       named_bar_sync(4 + k, 128);
-      // -- 3. softmax against the reference max, P' = P s_g E_g as hi + lo / 16 (two E4M3
-      //       terms; the residual is scaled by 16 to stay in E4M3's normal range) --
-      float alpha[4], gf[NG], mt[4], gm[NG];
+      // -- 3. lazy-rescale decisions: lane d = lane & 7 keeps m_ref of head 4k + d (d < 4) or
+      //       E of group d - 4 (d >= 4) in `st`, decides from the head set's table, and the
+      //       other lanes take the results by shuffle --
+      float fac = 1.f, pj[4];
+      bool resc;
+      {
+        const int d = lane & 7;
+        const float* tb = F + (d < 4 ? F_HMAX : F_GMAX) + (s * NG + k) * 16 + (d & 3);
+        const float v = fmaxf(fmaxf(tb[0], tb[4]), fmaxf(tb[8], tb[12]));
+        bool ch = false;
+        if (d < 4) {  // m_ref moves when the tile max exceeds it by more than kTau
+          if (v > st + kTau) {
+            fac = ex2_approx(st - v);
+            st = v;
+            ch = true;
+          }
+        } else if (i == 0) {
+          st = group_e(v);
+        } else if (v * st >= kEMax) {  // E_g moves when the largest scale times E_g reaches kEMax
+          const float en = group_e(v);
+          fac = pow2_ratio(en, st);
+          st = en;
+          ch = true;
+        }
+        resc = __any_sync(0xFFFFFFFFu, ch);
+        // P = 2^(s - m_ref) against the (possibly moved) reference max of each head
 #pragma unroll
-      for (int j = 0; j < 4; ++j)  // all table reads first: one shared-memory round trip
-        mt[j] = max4(*reinterpret_cast<const float4*>(F + F_HMAX + s * H * 4 + (4 * k + j) * 4));
-#pragma unroll
-      for (int g = 0; g < NG; ++g)
-        gm[g] = max4(*reinterpret_cast<const float4*>(F + F_GMAX + ((s * NG + k) * NG + g) * 4));
-      bool resc = false;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const bool up = mt[j] > m_ref[j] + kTau;
-        alpha[j] = up ? ex2_approx(m_ref[j] - mt[j]) : 1.f;
-        m_ref[j] = up ? mt[j] : m_ref[j];
-        resc |= up;
-      }
-#pragma unroll
-      for (int g = 0; g < NG; ++g) {  // branches are uniform: every thread sees the same tables
-        gf[g] = 1.f;
-        if (i == 0) {
-          E[g] = group_e(gm[g]);
-        } else if (gm[g] * E[g] >= kEMax) {
-          const float en = group_e(gm[g]);
-          gf[g] = pow2_ratio(en, E[g]);
-          E[g] = en;
-          resc = true;
+        for (int j = 0; j < 4; ++j) {
+          const float mr = __shfl_sync(0xFFFFFFFFu, st, j);
+          pj[j] = ok ? ex2_approx(s2[j] - mr) : 0.f;
         }
       }
       if (resc) {
+        float alpha[4], gf[NG];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) alpha[j] = __shfl_sync(0xFFFFFFFFu, fac, j);
+#pragma unroll
+        for (int g = 0; g < NG; ++g) gf[g] = __shfl_sync(0xFFFFFFFFu, fac, 4 + g);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           lsum[j] *= alpha[j];
@@ -565,16 +566,14 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc_fence_before();
         }
       }
-      float pj[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        pj[j] = ok ? ex2_approx(s2[j] - m_ref[j]) : 0.f;
-        lsum[j] += pj[j];
-      }
+      for (int j = 0; j < 4; ++j) lsum[j] += pj[j];
+      // -- 3b. P' = P s_g E_g as hi + lo / 16 (two E4M3 terms; the residual is scaled by 16 to
+      //        stay in E4M3's normal range); y sums exactly the value the tensor core sees --
       uint8_t* pb = smem + OFF_PB + s * PB_BUF;
 #pragma unroll
       for (int g = 0; g < NG; ++g) {
-        const float se = sc[g] * E[g];
+        const float se = sc[g] * __shfl_sync(0xFFFFFFFFu, st, 4 + g);
         uint32_t hw = 0, lw = 0;
 #pragma unroll
         for (int jp = 0; jp < 2; ++jp) {
@@ -637,6 +636,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
       for (int w = 0; w < 4; ++w) lt[j] += F[F_FINL + w * H + 4 * k + j];
     }
+    float m_ref[4], E[NG];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) m_ref[j] = __shfl_sync(0xFFFFFFFFu, st, j);
+#pragma unroll
+    for (int g = 0; g < NG; ++g) E[g] = __shfl_sync(0xFFFFFFFFu, st, 4 + g);
     if (q4 == 0 && lane == 0) {
 #pragma unroll
       for (int j = 0; j < 4; ++j)
