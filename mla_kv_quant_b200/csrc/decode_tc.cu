@@ -426,31 +426,27 @@ __global__ void __launch_bounds__(THREADS, 1)
         float2 A[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
         float2 B[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
         uint32_t pe[4];
+        uint32_t dq[NG][8];
 #pragma unroll
-        for (int g2 = 0; g2 < NG; g2 += 2) {  // two groups per TMEM round trip (register budget)
-          uint32_t dq[2][8];
-          tmem_ld8(tmem + lane_base + T_DQK + 32 * g2 + 8 * k, dq[0]);
-          tmem_ld8(tmem + lane_base + T_DQK + 32 * (g2 + 1) + 8 * k, dq[1]);
-          if (g2 == 0) tmem_ld4(tmem + lane_base + T_DPE + 4 * k, pe);
-          tmem_wait_ld();
-          reg_fence(dq[0]);
-          reg_fence(dq[1]);
-          if (g2 == 0) reg_fence(pe);
+        for (int g = 0; g < NG; ++g) tmem_ld8(tmem + lane_base + T_DQK + 32 * g + 8 * k, dq[g]);
+        tmem_ld4(tmem + lane_base + T_DPE + 4 * k, pe);
+        tmem_wait_ld();
 #pragma unroll
-          for (int gg = 0; gg < 2; ++gg) {
-            const int g = g2 + gg;
-            const float4 qs4 = *reinterpret_cast<const float4*>(F + F_QSUM + g * H + 4 * k);
-            const float2 qs[2] = {make_float2(qs4.x, qs4.y), make_float2(qs4.z, qs4.w)};
-            const float nscz = -sc[g] * zz[g];
+        for (int g = 0; g < NG; ++g) reg_fence(dq[g]);
+        reg_fence(pe);
 #pragma unroll
-            for (int jp = 0; jp < 2; ++jp) {
-              const uint32_t* d = dq[gg];  // hi terms d[0..3], lo terms d[4..7] (heads 4k..4k+3)
-              const float2 qc =
-                  make_float2(fmaf(__uint_as_float(d[4 + 2 * jp]), 0.0625f, __uint_as_float(d[2 * jp])),
-                              fmaf(__uint_as_float(d[5 + 2 * jp]), 0.0625f, __uint_as_float(d[2 * jp + 1])));
-              A[jp] = __ffma2_rn(make_float2(sc[g], sc[g]), qc, A[jp]);
-              B[jp] = __ffma2_rn(make_float2(nscz, nscz), qs[jp], B[jp]);
-            }
+        for (int g = 0; g < NG; ++g) {
+          const float4 qs4 = *reinterpret_cast<const float4*>(F + F_QSUM + g * H + 4 * k);
+          const float2 qs[2] = {make_float2(qs4.x, qs4.y), make_float2(qs4.z, qs4.w)};
+          const float nscz = -sc[g] * zz[g];
+#pragma unroll
+          for (int jp = 0; jp < 2; ++jp) {
+            const uint32_t* d = dq[g];
+            const float2 qc =
+                make_float2(fmaf(__uint_as_float(d[4 + 2 * jp]), 0.0625f, __uint_as_float(d[2 * jp])),
+                            fmaf(__uint_as_float(d[5 + 2 * jp]), 0.0625f, __uint_as_float(d[2 * jp + 1])));
+            A[jp] = __ffma2_rn(make_float2(sc[g], sc[g]), qc, A[jp]);
+            B[jp] = __ffma2_rn(make_float2(nscz, nscz), qs[jp], B[jp]);
           }
         }
         const float4 ki = *reinterpret_cast<const float4*>(F + F_KINV + 4 * k);
@@ -479,11 +475,6 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           tmem_st16(tmem + lane_base + T_AQK + 32 * k + 16 * hv, r);
         }
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(&bars[B_AQK]);  // A of QK^T(i+1) is in TMEM, D of QK^T(i) has been read
-      } else {
-        tc_fence_before();
       }
       // -- 2. the warp's tile maxima (its 32 tokens) of the four heads' scores and of the four
       //       group scales, one redux each, into the head set's table --
@@ -502,6 +493,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       // The four warps of head set k (one per token quarter) exchange their maxima; the head
       // sets do not wait for one another.  Each set's group-scale maxima cover all 128 tokens,
       // so every set takes the same E_g decisions.
+      if (i + 1 < ntiles) {  // the 1b stores, waited for after the maxima
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&bars[B_AQK]);  // A of QK^T(i+1) is in TMEM, D of QK^T(i) has been read
+      } else {
+        tc_fence_before();
+      }
       named_bar_sync(4 + k, 128);
       // -- 3. lazy-rescale decisions: lane d = lane & 7 keeps m_ref of head 4k + d (d < 4) or
       //       E of group d - 4 (d >= 4) in `st`, decides from the head set's table, and the
@@ -593,21 +591,22 @@ __global__ void __launch_bounds__(THREADS, 1)
       // -- 4. the PV-A tile of i+1 into buffer (i+1) & 1, last read by PV(i-1).  PV(i-1) is
       //       waited for on every tile (the last one too): PREADY(i) then cannot complete
       //       before the MMA warp has taken PREADY(i-1), so its parity wait never aliases. --
-      if (alive && i >= 1) alive = mbar_wait(&bars[B_PV], (i - 1) & 1, a.err);
       __syncwarp();  // the tcgen05.ld below is warp-collective
       if (i + 1 < ntiles) {
-        uint32_t r[32];  // the FP8 codes of tile i+1, as 1b wrote them to TMEM
-        tc_fence_after();
+        uint32_t r[32];  // the FP8 codes of tile i+1, as 1b wrote them to TMEM (read before the wait)
         tmem_ld32(tmem + lane_base + T_AQK + 32 * k, r);
         tmem_wait_ld();
         reg_fence(r);
-        tc_fence_before();
+        if (alive && i >= 1) alive = mbar_wait(&bars[B_PV], (i - 1) & 1, a.err);
+        tc_fence_after();
         store_pva((i + 1) & 1, r);
         ok = ok_next;
         if (i + 2 < ntiles) {
           load_tile(i + 2, pg_ahead);
           pg_ahead = page_raw(i + 3, t >> 6);
         }
+      } else if (alive && i >= 1) {
+        alive = mbar_wait(&bars[B_PV], (i - 1) & 1, a.err);
       }
       fence_proxy_async();
       mbar_arrive(&bars[B_PREADY]);  // P'(i), the PV-A tile of i+1 and a rescaled O are ready;
