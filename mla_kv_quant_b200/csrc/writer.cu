@@ -70,6 +70,7 @@ __device__ __noinline__ void exact_code_words(uint32_t taddr, float mean, float 
   for (int c = 0; c < 4; ++c) {
     tmem_ld32(taddr + c * 32, r);
     tmem_wait_ld();
+    reg_fence(r);
     uint32_t w0 = 0, w1 = 0;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
@@ -225,6 +226,7 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
         for (int c = 0; c < 4; ++c) {
           tmem_ld32(taddr + c * 32, r);
           tmem_wait_ld();
+          reg_fence(r);
           if (valid) {
             const int64_t col = group * 128 + c * 32;
             if (args.out_f32) {
@@ -253,6 +255,7 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
         for (int c = 0; c < 4; ++c) {
           tmem_ld32(taddr + c * 32, r);
           tmem_wait_ld();
+          reg_fence(r);
 #pragma unroll
           for (int j = 0; j < 32; ++j) acc.add(j & 7, __uint_as_float(r[j]));
         }
@@ -263,6 +266,7 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
         for (int c = 0; c < 4; ++c) {
           tmem_ld32(taddr + c * 32, r);
           tmem_wait_ld();
+          reg_fence(r);
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const float df = __fsub_rn(__uint_as_float(r[j]), mean);
@@ -291,6 +295,7 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
           for (int c = 0; c < 4; ++c) {
             tmem_ld32(taddr + c * 32, r);
             tmem_wait_ld();
+            reg_fence(r);
             uint32_t w0 = 0, w1 = 0;
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
@@ -339,6 +344,7 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
           for (int c = 0; c < 4; ++c) {
             tmem_ld32(taddr + c * 32, r);
             tmem_wait_ld();
+            reg_fence(r);
             if (hdst != nullptr) {
 #pragma unroll
               for (int j = 0; j < 4; ++j)
