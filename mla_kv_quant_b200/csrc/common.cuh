@@ -428,34 +428,20 @@ __device__ __forceinline__ float f32_next(float d) {
   return __int_as_float(d > 0.f ? b + 1 : b - 1);
 }
 
-// The smallest FP32 d with RN(d / std_) >= c, for finite std_ > 0.  RN(d / std_) does
-// not decrease as d grows, so [RN(diff / std_) >= c] == [diff >= bound] for every diff:
-// the Lloyd code [n >= -t] + [n >= 0] + [n >= t] becomes three compares per element with
-// the reference's IEEE-quotient semantics.  Returns false if the search did not settle
-// (then the caller falls back to the per-element quotient).
-__device__ __forceinline__ bool quotient_bound(float c, float std_, float* bound) {
-  float d = __fmul_rn(c, std_);
-  if (__fdiv_rn(d, std_) >= c) {
-#pragma unroll 1
-    for (int k = 0; k < 16; ++k) {
-      const float p = f32_prev(d);
-      if (!(__fdiv_rn(p, std_) >= c)) {
-        *bound = d;
-        return true;
-      }
-      d = p;
-    }
-  } else {
-#pragma unroll 1
-    for (int k = 0; k < 16; ++k) {
-      d = f32_next(d);
-      if (__fdiv_rn(d, std_) >= c) {
-        *bound = d;
-        return true;
-      }
-    }
-  }
-  return false;
+// The smallest FP32 d with RN(d / std_) >= c (IEEE quotient, round to nearest even), for
+// a normal c and 0 < std_ < 2^24.  RN(d / std_) does not decrease as d grows, so
+// [RN(diff / std_) >= c] == [diff >= bound] for every diff: the Lloyd code
+// [n >= -t] + [n >= 0] + [n >= t] becomes compares with the reference's IEEE-quotient
+// semantics.  RN(q) >= c exactly when q is above the midpoint m between c and the float
+// below it, or equal to it when c's last mantissa bit is even (the tie rounds to c).  m has
+// 25 significant bits, so m * std_ (<= 49 bits) is exact in FP64, and the bound is the
+// first float at or above it (one past it at an odd-c tie).
+__device__ __forceinline__ float quotient_bound(float c, float std_) {
+  const double m = (static_cast<double>(f32_prev(c)) + static_cast<double>(c)) * 0.5;
+  const double t = m * static_cast<double>(std_);
+  float b = __double2float_ru(t);
+  if (static_cast<double>(b) == t && (__float_as_uint(c) & 1u)) b = f32_next(b);
+  return b;
 }
 
 // The smallest FP32 d with RN(d / std_) >= 0, for 0 < std_ < 2^24: d / std_ rounds to -0

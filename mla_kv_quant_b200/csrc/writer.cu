@@ -1,19 +1,20 @@
 // Fused packed-INT2 cache writer for sm_100a.
 //
-// c = c_kv @ R runs on tcgen05 tensor cores: BF16 operands are staged in shared
-// memory by TMA (128-byte swizzle), one elected thread issues kind::f16 MMAs into one of
-// four FP32 accumulators in tensor memory, and four sets of four epilogue warps (one warp
-// per TMEM lane quarter) read the accumulators back (tcgen05.ld) to run the Lloyd INT2
-// codec, pack 4 codes per byte, scatter codes/params by slot, and write k_pe and the
-// s4r16 window rows.  Set s takes every fourth tile of the CTA, so the codec of four
-// tiles is in flight at once while the tensor core computes the next.
+// c = c_kv @ R runs on tcgen05 tensor cores: each CTA keeps the R^T slice of one
+// quantisation group resident in shared memory (loaded once by TMA, 128-byte swizzle) and
+// streams c_kv rows through a 3-stage ring of two 64-wide K chunks each; one elected thread
+// issues kind::f16 MMAs into one of four FP32 accumulators in tensor memory, and four sets
+// of four epilogue warps (one warp per TMEM lane quarter) read the accumulators back
+// (tcgen05.ld) to run the Lloyd INT2 codec, pack 4 codes per byte, scatter codes/params by
+// slot, and write k_pe and the s4r16 window rows.  Set s takes every fourth tile of the CTA,
+// so the codec of four tiles is in flight at once while the tensor core computes the next.
 //
 // Reference behaviour: deployment/sglang/QuantKernel/mla_fused_writer.py:54-224
 // (FP32 GEMM + Triton _pack_and_aux) and mla_quant/oscar.py:120-144 (codec).
 //
-// CTA tile: 128 rows x 128 latent columns = one quantisation group.  A row of D = 512 is
-// covered by four tiles; adjacent CTAs take the groups of the same rows, so the repeated
-// reads of those rows hit L2.
+// CTA tile: 128 rows x 128 latent columns = one quantisation group.  CTA c serves group
+// c % (D / 128) for every (#CTAs / groups)-th row tile, so the CTAs of one row tile run at
+// the same time and the repeated reads of its rows hit L2.
 #include "kernels.cuh"
 
 namespace rolaq {
@@ -21,16 +22,17 @@ namespace rolaq {
 constexpr int kTileM = 128;
 constexpr int kTileN = 128;  // one quantisation group
 constexpr int kTileK = 64;   // one 128-byte swizzle row of BF16
-constexpr int kStages = 6;
+constexpr int kStages = 3;
 constexpr int kABytes = kTileM * kTileK * 2;  // 16 KB
 constexpr int kBBytes = kTileN * kTileK * 2;  // 16 KB
-constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kStageBytes = 2 * kABytes;      // the ring streams c_kv only, two K chunks per stage
+constexpr int kMaxKChunks = 8;                // D <= 512: the group's R^T slice (<= 128 KB) stays resident
 constexpr int kNumBuf = 4;                       // TMEM accumulators = epilogue warp sets
 constexpr int kEpiWarps = 4 * kNumBuf;           // one warp per TMEM lane quarter per set
 constexpr int kWriterThreads = 32 * (2 + kEpiWarps);  // warp 0 TMA, warp 1 MMA, warps 2.. epilogue
 constexpr int kSetThreads = 128;
 constexpr uint32_t kTmemCols = kNumBuf * kTileN;  // 512
-constexpr size_t kWriterSmem = size_t(kStages) * kStageBytes + 1024 + 256;
+constexpr size_t kWriterSmem = size_t(kMaxKChunks) * kBBytes + size_t(kStages) * kStageBytes + 1024 + 256;
 
 // Per-row bookkeeping shared by the codec epilogue warps of one row.
 struct RowMeta {
@@ -39,9 +41,8 @@ struct RowMeta {
   bool ok;       // slot in range
 };
 
-__device__ __forceinline__ RowMeta row_meta(const WriterArgs& a, int64_t row) {
+__device__ __forceinline__ RowMeta row_meta(const WriterArgs& a, int64_t row, int64_t slot) {
   RowMeta m{0, -1, false};
-  const int64_t slot = a.slots[row];
   m.slot = slot;
   m.ok = slot >= 0 && slot < a.cache.num_slots;
   const int P = a.cache.sink, W = a.cache.recent;
@@ -59,6 +60,41 @@ __device__ __forceinline__ RowMeta row_meta(const WriterArgs& a, int64_t row) {
     }
   }
   return m;
+}
+
+// FP32 set: -1 when a >= b, else 0 (one instruction).
+__device__ __forceinline__ int set_ge(float a, float b) {
+  int r;
+  asm("set.ge.s32.f32 %0, %1, %2;" : "=r"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// The smallest FP32 x with RN(x - m) >= b.  RN(x - m) never decreases as x grows, so
+// [RN(x - m) >= b] is [x >= X]; X lies within a few ulps of RN(b + m).  False when the walk
+// does not settle (the caller then takes the per-element path).
+__device__ __forceinline__ bool sub_bound(float b, float m, float* X) {
+  float x = __fadd_rn(b, m);
+  if (__fsub_rn(x, m) >= b) {
+#pragma unroll 1
+    for (int k = 0; k < 16; ++k) {
+      const float p = f32_prev(x);
+      if (!(__fsub_rn(p, m) >= b)) {
+        *X = x;
+        return true;
+      }
+      x = p;
+    }
+  } else {
+#pragma unroll 1
+    for (int k = 0; k < 16; ++k) {
+      x = f32_next(x);
+      if (__fsub_rn(x, m) >= b) {
+        *X = x;
+        return true;
+      }
+    }
+  }
+  return false;
 }
 
 // Codes of one (row, 128-group) from the IEEE quotient per element: the reference's
@@ -92,11 +128,14 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint8_t* bres = smem;                          // R^T slice of the CTA's group: kchunks x 16 KB
+  uint8_t* ring = smem + kMaxKChunks * kBBytes;  // c_kv stages
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + kStages * kStageBytes);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + kNumBuf;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + kNumBuf);
+  uint64_t* bfull = tempty + kNumBuf;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bfull + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -104,8 +143,12 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
   const int d = args.d;
   const int groups = d / kTileN;
   const int64_t row_tiles = (args.n + kTileM - 1) / kTileM;
-  const int64_t tiles = row_tiles * groups;
   const int kchunks = d / kTileK;
+  // One group per CTA (its R^T slice resident in shared memory): CTA c takes group c % groups
+  // and the row tiles c / groups, + ctas_g, ...
+  const int group = static_cast<int>(blockIdx.x % groups);
+  const int64_t cg = blockIdx.x / groups;
+  const int64_t ctas_g = (gridDim.x - group + groups - 1) / groups;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -116,6 +159,7 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], kSetThreads);
     }
+    mbar_init(bfull, 1);
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tensormap(&tmap_x);
@@ -133,21 +177,22 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
   if (warp == 0) {
     // ---- TMA producer -------------------------------------------------------------
     if (lane == 0) {
+      mbar_expect_tx(bfull, static_cast<uint32_t>(kchunks * kBBytes));
+      for (int kc = 0; kc < kchunks; ++kc)
+        tma_load_2d(bres + kc * kBBytes, &tmap_w, bfull, kc * kTileK, group * kTileN);
       int stage = 0;
       uint32_t phase = 0;
-      for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
-        const int32_t row0 = static_cast<int32_t>((t / groups) * kTileM);
-        const int32_t col0 = static_cast<int32_t>((t % groups) * kTileN);
-        for (int kc = 0; kc < kchunks; ++kc) {
+      for (int64_t rt = cg; rt < row_tiles; rt += ctas_g) {
+        const int32_t row0 = static_cast<int32_t>(rt * kTileM);
+        for (int kc = 0; kc < kchunks; kc += 2) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, args.err)) {
             *abort_flag = 1;
             break;
           }
-          uint8_t* a_s = smem + stage * kStageBytes;
-          uint8_t* b_s = a_s + kABytes;
+          uint8_t* a_s = ring + stage * kStageBytes;
           mbar_expect_tx(&full[stage], kStageBytes);
           tma_load_2d(a_s, &tmap_x, &full[stage], kc * kTileK, row0);
-          tma_load_2d(b_s, &tmap_w, &full[stage], kc * kTileK, col0);
+          tma_load_2d(a_s + kABytes, &tmap_x, &full[stage], (kc + 1) * kTileK, row0);
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
@@ -162,29 +207,38 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       const uint32_t idesc = idesc_bf16(kTileM, kTileN);
+      // Descriptors formed once: operands sit at fixed offsets from the ring and the resident
+      // slice, and the 14-bit start-address field (addr >> 4) never carries within shared
+      // memory, so each MMA's descriptors are the bases plus constants (two adds per MMA: the
+      // issuing thread shares its sub-partition with epilogue warps).
+      const uint64_t da0 = sw128_kmajor_desc(smem_u32(ring));
+      const uint64_t db0 = sw128_kmajor_desc(smem_u32(bres));
+      bool ok = mbar_wait(bfull, 0, args.err);
       int64_t lt = 0;
-      for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++lt) {
+      for (int64_t rt = cg; ok && rt < row_tiles; rt += ctas_g, ++lt) {
         const int buf = static_cast<int>(lt % kNumBuf);
         const uint32_t use = static_cast<uint32_t>(lt / kNumBuf);
         if (!mbar_wait(&tempty[buf], (use & 1u) ^ 1u, args.err)) {
-          *abort_flag = 1;
+          ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kTileN);
-        bool ok = true;
-        for (int kc = 0; kc < kchunks; ++kc) {
+        for (int kc = 0; kc < kchunks; kc += 2) {
           if (!mbar_wait(&full[stage], phase, args.err)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + stage * kStageBytes);
-          const uint32_t b_addr = a_addr + kABytes;
+          const uint64_t da = da0 + static_cast<uint64_t>((stage * kStageBytes) >> 4);
+          const uint64_t db = db0 + static_cast<uint64_t>((kc * kBBytes) >> 4);
 #pragma unroll
-          for (int k = 0; k < kTileK / 16; ++k) {
-            umma_bf16_ss(d_tmem, sw128_kmajor_desc(a_addr + k * 32), sw128_kmajor_desc(b_addr + k * 32), idesc,
-                         (kc | k) != 0);
+          for (int h = 0; h < 2; ++h) {
+#pragma unroll
+            for (int k = 0; k < kTileK / 16; ++k) {
+              umma_bf16_ss(d_tmem, da + static_cast<uint64_t>((h * kABytes + k * 32) >> 4),
+                           db + static_cast<uint64_t>((h * kBBytes + k * 32) >> 4), idesc, (kc | h | k) != 0);
+            }
           }
           umma_commit(&empty[stage]);
           if (++stage == kStages) {
@@ -192,12 +246,10 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
             phase ^= 1u;
           }
         }
-        if (!ok) {
-          *abort_flag = 1;
-          break;
-        }
+        if (!ok) break;
         umma_commit(&tfull[buf]);
       }
+      if (!ok) *abort_flag = 1;
     }
   } else {
     // ---- epilogue: set (w-2)/4 takes tiles lt = set, set + 4, ...; warp w reads TMEM lanes
@@ -205,8 +257,7 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
     const int quad = warp & 3;
     const int set = (warp - 2) >> 2;
     int64_t lt = set;
-    for (int64_t t = blockIdx.x + set * static_cast<int64_t>(gridDim.x); t < tiles;
-         t += kNumBuf * static_cast<int64_t>(gridDim.x), lt += kNumBuf) {
+    for (int64_t rt = cg + set * ctas_g; rt < row_tiles; rt += kNumBuf * ctas_g, lt += kNumBuf) {
       const int buf = static_cast<int>(lt % kNumBuf);
       const uint32_t use = static_cast<uint32_t>(lt / kNumBuf);
       if (!mbar_wait(&tfull[buf], use & 1u, args.err)) {
@@ -214,8 +265,7 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
         break;
       }
       tc_fence_after();
-      const int64_t row = (t / groups) * kTileM + quad * 32 + lane;
-      const int group = static_cast<int>(t % groups);
+      const int64_t row = rt * kTileM + quad * 32 + lane;
       const bool valid = row < args.n;
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(buf * kTileN);
@@ -278,15 +328,21 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
         const float thr = args.codec.threshold;
         // pass 3: codes.  n = RN(diff / std) never decreases as diff grows, so each of the
         // reference's tests [n >= -t], [n >= 0], [n >= t] is diff >= an exact FP32 bound
-        // found once per (row, group) with the IEEE quotient (the middle one in closed form);
-        // a std of 2^24 or more, or a bound search that does not settle, takes the
+        // found once per (row, group) (FP64 midpoint products; the middle one in closed
+        // form), and diff = RN(x - mean) >= b is x >= X(b): three compares on the raw value
+        // per element.  A std of 2^24 or more, or a search that does not settle, takes the
         // per-element quotient instead.
         float b_lo = 0.f, b_mid = 0.f, b_hi = 0.f;
         bool exact_all = !(stdv < 16777216.f);
         if (!exact_all) {
           b_mid = quotient_bound_zero(stdv);
-          exact_all = !(quotient_bound(-thr, stdv, &b_lo) && quotient_bound(thr, stdv, &b_hi));
+          b_lo = quotient_bound(-thr, stdv);
+          b_hi = quotient_bound(thr, stdv);
         }
+        float x_lo = 0.f, x_mid = 0.f, x_hi = 0.f;
+        if (!exact_all)
+          exact_all = !(sub_bound(b_lo, mean, &x_lo) && sub_bound(b_mid, mean, &x_mid) &&
+                        sub_bound(b_hi, mean, &x_hi));
         uint32_t words[8];
         if (__any_sync(0xFFFFFFFFu, exact_all)) {
           exact_code_words(taddr, mean, stdv, thr, words);  // rare: the whole warp, quotient per element
@@ -299,13 +355,12 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
             uint32_t w0 = 0, w1 = 0;
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              const float df = __fsub_rn(__uint_as_float(r[j]), mean);
-              const uint32_t code = static_cast<uint32_t>(df >= b_lo) + static_cast<uint32_t>(df >= b_mid) +
-                                    static_cast<uint32_t>(df >= b_hi);
+              const float x = __uint_as_float(r[j]);
+              const int ncode = set_ge(x, x_lo) + set_ge(x, x_mid) + set_ge(x, x_hi);  // -code
               if (j < 16)
-                w0 |= code << (2 * j);
+                w0 -= static_cast<uint32_t>(ncode) << (2 * j);
               else
-                w1 |= code << (2 * (j - 16));
+                w1 -= static_cast<uint32_t>(ncode) << (2 * (j - 16));
             }
             words[2 * c] = w0;
             words[2 * c + 1] = w1;
@@ -314,7 +369,7 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
         const float scale = __fmul_rn(args.codec.scale_factor, stdv);
         const float zero = __fsub_rn(args.codec.zero_const, __fdiv_rn(mean, scale));
         RowMeta m{0, -1, false};
-        if (valid) m = row_meta(args, row);
+        if (valid) m = row_meta(args, row, args.slots[row]);
         if (valid && !m.ok && group == 0) report(args.err, ROLAQ_DEV_BAD_SLOT);
         if (valid && m.ok) {
           uint4* cdst = reinterpret_cast<uint4*>(args.cache.codes + m.slot * (d / 4) + group * 32);
@@ -393,6 +448,7 @@ int launch_writer(const uint16_t* x, int64_t ldx, const uint16_t* w, const Write
   CUtensorMap mx, mw;
   const int d = args.d;
   if (args.n <= 0) return ROLAQ_OK;
+  if (d % (2 * kTileK) != 0 || d / kTileK > kMaxKChunks) return ROLAQ_EUNSUPPORTED;
   int rc = make_map_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, static_cast<uint64_t>(d),
                        static_cast<uint64_t>(args.n), static_cast<uint64_t>(ldx) * 2, kTileK, kTileM);
   if (rc != ROLAQ_OK) return rc;
