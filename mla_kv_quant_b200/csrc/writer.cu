@@ -41,16 +41,18 @@ struct RowMeta {
   bool ok;       // slot in range
 };
 
-__device__ __forceinline__ RowMeta row_meta(const WriterArgs& a, int64_t row, int64_t slot) {
+// A row's slot check and ring row (window rules of the reference writer: sink positions and
+// the last `recent` positions keep a BF16 copy in the request's ring), from its slot, seq
+// length, request index and position (ignored when the call gives no positions: seq - 1).
+__device__ __forceinline__ RowMeta row_meta_of(const WriterArgs& a, int64_t slot, int64_t seq, int64_t req,
+                                               int64_t pos_or_neg1) {
   RowMeta m{0, -1, false};
   m.slot = slot;
   m.ok = slot >= 0 && slot < a.cache.num_slots;
   const int P = a.cache.sink, W = a.cache.recent;
   if (m.ok && slot > 0 && a.seq_lens != nullptr && a.req_idx != nullptr && a.cache.rows != nullptr &&
       (P + W) > 0) {
-    const int64_t seq = load_index(a.seq_lens, a.seq_is64, row);
-    const int64_t req = load_index(a.req_idx, a.req_is64, row);
-    const int64_t pos = a.positions ? load_index(a.positions, a.pos_is64, row) : seq - 1;
+    const int64_t pos = a.positions ? pos_or_neg1 : seq - 1;
     const bool keep = (pos < P || pos >= seq - W) && req >= 0 && req < a.cache.max_reqs && pos >= 0;
     if (keep) {
       const int64_t w = W > 0 ? W : 1;
@@ -60,6 +62,17 @@ __device__ __forceinline__ RowMeta row_meta(const WriterArgs& a, int64_t row, in
     }
   }
   return m;
+}
+
+__device__ __forceinline__ RowMeta row_meta(const WriterArgs& a, int64_t row, int64_t slot) {
+  int64_t seq = 0, req = 0, pos = -1;
+  if (slot > 0 && slot < a.cache.num_slots && a.seq_lens != nullptr && a.req_idx != nullptr &&
+      a.cache.rows != nullptr) {
+    seq = load_index(a.seq_lens, a.seq_is64, row);
+    req = load_index(a.req_idx, a.req_is64, row);
+    if (a.positions != nullptr) pos = load_index(a.positions, a.pos_is64, row);
+  }
+  return row_meta_of(a, slot, seq, req, pos);
 }
 
 // FP32 set: -1 when a >= b, else 0 (one instruction).
@@ -425,6 +438,172 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
   }
 }
 
+
+// ---- small batches (decode writes): SIMT rotation + codec -------------------------------
+//
+// For n <= kSmallWriteRows the tensor-core pipeline above is all fill and drain (one tile
+// per group), so a CTA per (4 rows, group) computes its 4 x 128 rotated values with FP32
+// FMAs (thread: one output column over one quarter of K in increasing k, its R^T loads all
+// issued before the first FMA; the quarters added in order) and one warp per row runs the
+// codec in the oracle's order: lane k < 8 keeps the
+// running sum acc[k] over columns k, k + 8, .., and the tree
+// ((a0+a1)+(a2+a3))+((a4+a5)+(a6+a7)) is the xor-1, -2, -4 shuffle pairing.  The codes
+// come from the same exact bounds as the tensor-core path; rolaq_rotate_rows takes the same
+// path for the same n, so a batch's codes always match its own rotated values.
+constexpr int kSmRows = 4;
+constexpr int kSmThreads = 512;  // 128 output columns x 4 quarters of K
+constexpr int64_t kSmallWriteRows = 256;
+
+template <bool kPlain>
+__global__ void __launch_bounds__(kSmThreads) small_writer_kernel(const uint16_t* __restrict__ x, int64_t ldx,
+                                                                  const uint16_t* __restrict__ w,
+                                                                  const WriterArgs args) {
+  __shared__ __align__(16) float xs[kSmRows][512];
+  __shared__ float part[3][kSmRows][kTileN];
+  __shared__ float cs[kSmRows][kTileN];
+  const int d = args.d;
+  const int group = blockIdx.y;
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kSmRows;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // Every independent global load is issued here, before any of them is used: this thread's
+  // R^T quarter row, its 16-byte piece of the block's rows, and (lane 0 of warp r) row r's
+  // slot and window metadata.
+  const int col = tid & (kTileN - 1), quarter = tid >> 7, kq = d / 4;  // kq <= 128
+  const uint16_t* wr = w + static_cast<int64_t>(group * kTileN + col) * d + quarter * kq;
+  uint4 wv[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    if (8 * i < kq) wv[i] = *reinterpret_cast<const uint4*>(wr + 8 * i);
+  static_assert(kSmThreads >= kSmRows * 512 / 8, "one 16-byte piece of the rows per thread");
+  const int xr = tid / (d / 8), xk8 = tid % (d / 8);
+  uint4 xv = make_uint4(0, 0, 0, 0);
+  if (xr < kSmRows && row0 + xr < args.n) xv = *reinterpret_cast<const uint4*>(x + (row0 + xr) * ldx + 8 * xk8);
+  int64_t m_slot = 0, m_seq = 0, m_req = 0, m_pos = -1;
+  if (!kPlain && warp < kSmRows && lane == 0 && row0 + warp < args.n) {
+    const int64_t row = row0 + warp;
+    m_slot = args.slots[row];
+    if (args.seq_lens != nullptr) m_seq = load_index(args.seq_lens, args.seq_is64, row);
+    if (args.req_idx != nullptr) m_req = load_index(args.req_idx, args.req_is64, row);
+    if (args.positions != nullptr) m_pos = load_index(args.positions, args.pos_is64, row);
+  }
+  if (xr < kSmRows) {  // the block's rows as FP32
+    const uint32_t ws[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      xs[xr][8 * xk8 + 2 * c] = bf16_lo(ws[c]);
+      xs[xr][8 * xk8 + 2 * c + 1] = bf16_hi(ws[c]);
+    }
+  }
+  __syncthreads();
+  {
+    float acc[kSmRows];
+#pragma unroll
+    for (int r = 0; r < kSmRows; ++r) acc[r] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      if (8 * i >= kq) break;
+      const float wf[8] = {bf16_lo(wv[i].x), bf16_hi(wv[i].x), bf16_lo(wv[i].y), bf16_hi(wv[i].y),
+                           bf16_lo(wv[i].z), bf16_hi(wv[i].z), bf16_lo(wv[i].w), bf16_hi(wv[i].w)};
+#pragma unroll
+      for (int r = 0; r < kSmRows; ++r) {
+        const float4 x0 = *reinterpret_cast<const float4*>(&xs[r][quarter * kq + 8 * i]);
+        const float4 x1 = *reinterpret_cast<const float4*>(&xs[r][quarter * kq + 8 * i + 4]);
+        acc[r] = fmaf(x0.x, wf[0], acc[r]);
+        acc[r] = fmaf(x0.y, wf[1], acc[r]);
+        acc[r] = fmaf(x0.z, wf[2], acc[r]);
+        acc[r] = fmaf(x0.w, wf[3], acc[r]);
+        acc[r] = fmaf(x1.x, wf[4], acc[r]);
+        acc[r] = fmaf(x1.y, wf[5], acc[r]);
+        acc[r] = fmaf(x1.z, wf[6], acc[r]);
+        acc[r] = fmaf(x1.w, wf[7], acc[r]);
+      }
+    }
+    if (quarter > 0) {
+#pragma unroll
+      for (int r = 0; r < kSmRows; ++r) part[quarter - 1][r][col] = acc[r];
+    }
+    __syncthreads();
+    if (quarter == 0) {
+#pragma unroll
+      for (int r = 0; r < kSmRows; ++r)
+        cs[r][col] = __fadd_rn(__fadd_rn(__fadd_rn(acc[r], part[0][r][col]), part[1][r][col]), part[2][r][col]);
+    }
+    __syncthreads();
+  }
+  if (warp >= kSmRows) return;
+  const int64_t row = row0 + warp;
+  if (row >= args.n) return;  // whole warp
+  const float* c = cs[warp];
+  const float4 v4 = *reinterpret_cast<const float4*>(c + 4 * lane);  // this lane's columns 4l .. 4l + 3
+  const float v[4] = {v4.x, v4.y, v4.z, v4.w};
+  if constexpr (kPlain) {
+    const int64_t col = group * kTileN + 4 * lane;
+    if (args.out_f32) *reinterpret_cast<float4*>(args.out_f32 + row * args.ld_out + col) = v4;
+    if (args.out_bf16)
+      *reinterpret_cast<uint2*>(args.out_bf16 + row * args.ld_out + col) =
+          make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
+    return;
+  } else {
+    // group sums in the fixed order (lanes 0..7 hold the running sums, the tree by shuffles)
+    auto group_total = [&](auto term) {
+      float a = 0.f;
+      if (lane < 8) {
+#pragma unroll
+        for (int i = 0; i < kTileN / 8; ++i) a = __fadd_rn(a, term(c[8 * i + lane]));
+      }
+      const float t1 = __fadd_rn(a, __shfl_xor_sync(0xFFFFFFFFu, a, 1));
+      const float t2 = __fadd_rn(t1, __shfl_xor_sync(0xFFFFFFFFu, t1, 2));
+      const float t3 = __fadd_rn(t2, __shfl_xor_sync(0xFFFFFFFFu, t2, 4));
+      return __shfl_sync(0xFFFFFFFFu, t3, 0);
+    };
+    const float mean = __fmul_rn(group_total([](float x) { return x; }), 1.0f / 128.0f);
+    const float var = __fmul_rn(group_total([&](float x) {
+                                  const float df = __fsub_rn(x, mean);
+                                  return __fmul_rn(df, df);
+                                }), 1.0f / 128.0f);
+    const float stdv = __fsqrt_rn(__fadd_rn(var, 1e-8f));
+    const float thr = args.codec.threshold;
+    uint32_t byte = 0;
+    if (stdv < 16777216.f) {  // exact bounds: three compares per element
+      const float b_lo = quotient_bound(-thr, stdv), b_mid = quotient_bound_zero(stdv),
+                  b_hi = quotient_bound(thr, stdv);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float df = __fsub_rn(v[q], mean);
+        byte |= (static_cast<uint32_t>(df >= b_lo) + static_cast<uint32_t>(df >= b_mid) +
+                 static_cast<uint32_t>(df >= b_hi)) << (2 * q);
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) byte |= lloyd_code(__fsub_rn(v[q], mean), stdv, thr) << (2 * q);
+    }
+    const float scale = __fmul_rn(args.codec.scale_factor, stdv);
+    const float zero = __fsub_rn(args.codec.zero_const, __fdiv_rn(mean, scale));
+    const RowMeta m = row_meta_of(args, __shfl_sync(0xFFFFFFFFu, m_slot, 0), __shfl_sync(0xFFFFFFFFu, m_seq, 0),
+                                  __shfl_sync(0xFFFFFFFFu, m_req, 0), __shfl_sync(0xFFFFFFFFu, m_pos, 0));
+    if (!m.ok) {
+      if (group == 0 && lane == 0) report(args.err, ROLAQ_DEV_BAD_SLOT);
+      return;
+    }
+    args.cache.codes[m.slot * (d / 4) + group * 32 + lane] = static_cast<uint8_t>(byte);
+    if (lane == 0)
+      *reinterpret_cast<float2*>(args.cache.params + (m.slot * (d / 128) + group) * 2) = make_float2(scale, zero);
+    if (group == 0 && m.slot > 0) {
+      const int dr = args.cache.rope_dim;
+      if (args.k_pe != nullptr && lane < dr / 8)
+        reinterpret_cast<uint4*>(args.cache.rope + m.slot * dr)[lane] =
+            reinterpret_cast<const uint4*>(args.k_pe + row * args.ld_pe)[lane];
+      if (lane == 0 && args.cache.rows != nullptr && args.seq_lens != nullptr && args.req_idx != nullptr) {
+        args.cache.rows[m.slot] = static_cast<int32_t>(m.ring);
+        if (m.ring >= 0) args.cache.owners[m.ring] = static_cast<int32_t>(m.slot);
+      }
+    }
+    if (m.ring >= 0)  // window row: the BF16 rotated latent into the ring
+      *reinterpret_cast<uint2*>(args.cache.hp + m.ring * d + group * kTileN + 4 * lane) =
+          make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
+  }
+}
+
 // ---- host side -----------------------------------------------------------------------
 
 // 2-D BF16 (or byte) tensor map over a row-major matrix, 128-byte swizzle.
@@ -449,6 +628,14 @@ int launch_writer(const uint16_t* x, int64_t ldx, const uint16_t* w, const Write
   const int d = args.d;
   if (args.n <= 0) return ROLAQ_OK;
   if (d % (2 * kTileK) != 0 || d / kTileK > kMaxKChunks) return ROLAQ_EUNSUPPORTED;
+  if (args.n <= kSmallWriteRows) {
+    const dim3 grid(static_cast<unsigned>((args.n + kSmRows - 1) / kSmRows), static_cast<unsigned>(d / kTileN));
+    if (plain)
+      small_writer_kernel<true><<<grid, kSmThreads, 0, stream>>>(x, ldx, w, args);
+    else
+      small_writer_kernel<false><<<grid, kSmThreads, 0, stream>>>(x, ldx, w, args);
+    return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;
+  }
   int rc = make_map_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, static_cast<uint64_t>(d),
                        static_cast<uint64_t>(args.n), static_cast<uint64_t>(ldx) * 2, kTileK, kTileM);
   if (rc != ROLAQ_OK) return rc;
