@@ -220,6 +220,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   };
 
+  // token threads: the page ids of tiles 0 and 1, loaded before the set-up (their latency
+  // overlaps the query preparation)
+  int32_t raw0 = 0, raw1 = 0;
+  if (warp < NTOK_WARPS) {
+    raw0 = page_raw(0, (32 * (warp & 3) + lane) >> 6);
+    raw1 = page_raw(1, (32 * (warp & 3) + lane) >> 6);
+  }
   // ---- set-up ---------------------------------------------------------------------------
   if (tid == 0) {
     mbar_init(&bars[B_KPE], 1);
@@ -276,16 +283,23 @@ __global__ void __launch_bounds__(THREADS, 1)
     if ((part & 7) == 0) F[F_QSUM + g * H + h] = sum;
     uint8_t* qb = smem + OFF_QB + g * QB_GROUP;
     const int row_hi = 8 * (h >> 2) + (h & 3), row_lo = row_hi + 4;
+    // The 16 elements fill one 16-byte chunk of each row in the K order of the code bytes:
+    // byte j holds element kperm(j) = 4 (j & 3) + (j >> 2), so word w holds elements w, w + 4,
+    // w + 8, w + 12 (all of w's parity, hence one weight).
+    uint32_t hw[4], lw[4];
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const int kk = kperm(16 * (part & 7) + e);
-      const float x = v[e] * qs * ((e & 1) ? 0.25f : 1.f);
-      const uint32_t hq = f32x2_to_e4m3x2(x, 0.f) & 0xFFu;
-      const float hf = __low2float(e4m3x2_to_half2(hq));
-      const uint32_t lq = f32x2_to_e4m3x2((x - hf) * 16.f, 0.f) & 0xFFu;
-      qb[sw128(row_hi, kk)] = static_cast<uint8_t>(hq);
-      qb[sw128(row_lo, kk)] = static_cast<uint8_t>(lq);
+    for (int w = 0; w < 4; ++w) {
+      const float sw = qs * ((w & 1) ? 0.25f : 1.f);
+      const float x0 = v[w] * sw, x1 = v[w + 4] * sw, x2 = v[w + 8] * sw, x3 = v[w + 12] * sw;
+      const uint32_t h01 = f32x2_to_e4m3x2(x0, x1), h23 = f32x2_to_e4m3x2(x2, x3);
+      const __half2 f01 = e4m3x2_to_half2(h01), f23 = e4m3x2_to_half2(h23);
+      const uint32_t l01 = f32x2_to_e4m3x2((x0 - __low2float(f01)) * 16.f, (x1 - __high2float(f01)) * 16.f);
+      const uint32_t l23 = f32x2_to_e4m3x2((x2 - __low2float(f23)) * 16.f, (x3 - __high2float(f23)) * 16.f);
+      hw[w] = __byte_perm(h01, h23, 0x5410);
+      lw[w] = __byte_perm(l01, l23, 0x5410);
     }
+    *reinterpret_cast<uint4*>(qb + sw128(row_hi, 16 * (part & 7))) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4*>(qb + sw128(row_lo, 16 * (part & 7))) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     if (part < 8) {  // rope part of the query: BF16 row of 64 into a K-major SW128 tile
       const uint4 w = *reinterpret_cast<const uint4*>(qh + D + 8 * part);
       *reinterpret_cast<uint4*>(smem + OFF_QPE + sw128(h, 16 * part)) = w;
@@ -378,8 +392,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             make_uint4(r[4 * kq], r[4 * kq + 1], r[4 * kq + 2], r[4 * kq + 3]);
     };
     // prologue: tile 0 into TMEM and PV-A buffer 0, QK^T(0)
-    load_tile(0, page_raw(0, t >> 6));
-    int32_t pg_ahead = page_raw(1, t >> 6);  // page id of tile i + 2 (in the loop)
+    load_tile(0, raw0);
+    int32_t pg_ahead = raw1;  // page id of tile i + 2 (in the loop)
     {
       uint32_t r[32];
       expand(r);
@@ -651,6 +665,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncwarp();
     tc_fence_after();
     const float rs = ((t >> 2) & 1) ? 128.f : 512.f;  // 2^9 / (1 or 4): the element's code weight
+    float il[4], ie[NG];  // 1 / sum P per head (0 for an empty split), 1 / E_g (exact: powers of two)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) il[j] = lt[j] > 0.f ? 1.f / lt[j] : 0.f;
+#pragma unroll
+    for (int g = 0; g < NG; ++g) ie[g] = 1.f / E[g];
     float* po = a.part_o + (static_cast<int64_t>(b) * H * S + split) * D + kperm(t);
     const int hs = S * D;  // head stride of part_o
 #pragma unroll
@@ -665,7 +684,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int w = 0; w < 4; ++w) yy += F[F_FINY + (w * NG + g) * H + 4 * k + j];
         const float dh = fmaf(__uint_as_float(v[4 + j]), 0.0625f, __uint_as_float(v[j]));
-        po[(4 * k + j) * hs + 128 * g] = lt[j] > 0.f ? (dh * rs - yy) / (E[g] * lt[j]) : 0.f;
+        po[(4 * k + j) * hs + 128 * g] = (dh * rs - yy) * (il[j] * ie[g]);
       }
     }
     tc_fence_before();
