@@ -626,20 +626,41 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_arrive(&bars[B_PREADY]);  // P'(i), the PV-A tile of i+1 and a rescaled O are ready;
                                      // params stage i & 1 has been read
     }
-    // -- final: sum P and sum P' z over the warp's 32 tokens --
+    // -- final: sum P and sum P' z over the warp's 32 tokens.  Transposed butterfly: at the
+    //    xor-16, 8, 4, 2 steps each lane keeps half of its remaining values and adds its
+    //    partner's copy of them (the same pairing per value as five plain xor steps), so a
+    //    value ends in the lanes whose bits 4..1 spell its index --
+    {
+      float v[16];  // y[g][j] at index 4g + j
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float l = lsum[j];
+      for (int g = 0; g < NG; ++g)
 #pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
-      if (lane == 0) F[F_FINL + q4 * H + 4 * k + j] = l;
+        for (int j = 0; j < 4; ++j) v[4 * g + j] = y[g][j];
 #pragma unroll
-      for (int g = 0; g < NG; ++g) {
-        float yy = y[g][j];
+      for (int half = 8, o = 16; half >= 1; half >>= 1, o >>= 1) {
+        const bool up = (lane & o) != 0;
 #pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) yy += __shfl_xor_sync(0xFFFFFFFFu, yy, o);
-        if (lane == 0) F[F_FINY + (q4 * NG + g) * H + 4 * k + j] = yy;
+        for (int i = 0; i < half; ++i) {
+          const float keep = up ? v[i + half] : v[i], send = up ? v[i] : v[i + half];
+          v[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, o);
+        }
       }
+      v[0] += __shfl_xor_sync(0xFFFFFFFFu, v[0], 1);
+      const int idx = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+      if ((lane & 1) == 0) F[F_FINY + (q4 * NG + (idx >> 2)) * H + 4 * k + (idx & 3)] = v[0];
+      float l[4] = {lsum[0], lsum[1], lsum[2], lsum[3]};
+#pragma unroll
+      for (int half = 2, o = 16; half >= 1; half >>= 1, o >>= 1) {
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+          const float keep = up ? l[i + half] : l[i], send = up ? l[i] : l[i + half];
+          l[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, o);
+        }
+      }
+#pragma unroll
+      for (int o = 4; o >= 1; o >>= 1) l[0] += __shfl_xor_sync(0xFFFFFFFFu, l[0], o);
+      if ((lane & 7) == 0) F[F_FINL + q4 * H + 4 * k + ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1)] = l[0];
     }
     named_bar_sync(3, TOK_THREADS);
     float lt[4];  // sum P over the split per head 4k + j
