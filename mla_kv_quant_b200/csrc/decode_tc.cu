@@ -76,8 +76,8 @@ constexpr int F_KINV = F_QSUM + NG * H;  // [H]         2^(9 - k_h)
 constexpr int F_HMAX = F_KINV + H;       // [2][NG][4][4] tile max per head set, token quarter, head
 constexpr int F_GMAX = F_HMAX + 2 * H * 4;        // [2][NG][4][NG] tile max of s_g per head set,
                                                   //                token quarter and group
-constexpr int F_FINL = F_GMAX + 2 * NG * NG * 4;  // [4][H]      sum P per token quarter
-constexpr int F_FINY = F_FINL + 4 * H;       // [4][NG][H]  sum P' z per token quarter
+constexpr int F_FINL = F_GMAX + 2 * NG * NG * 4;  // [H][4]      sum P per head and token quarter
+constexpr int F_FINY = F_FINL + 4 * H;       // [NG][H][4]  sum P' z per group, head and token quarter
 constexpr int F_TOTAL = F_FINY + 4 * NG * H;
 constexpr int OFF_BAR = OFF_F + ((F_TOTAL * 4 + 15) / 16) * 16;
 // B_KFREE[s]: QK^T of the tile in k_pe stage s has completed (producer may refill it);
@@ -89,7 +89,8 @@ constexpr int OFF_TMEMSLOT = OFF_BAR + N_BARS * 8;
 constexpr size_t SMEM = size_t(OFF_TMEMSLOT) + 16 + 1024;
 static_assert(SMEM <= 227 * 1024, "shared memory budget");
 static_assert(kEMax * 22.7f < 448.f, "P' must stay below the largest E4M3 value");
-static_assert(F_HMAX % 4 == 0 && F_GMAX % 4 == 0 && F_QSUM % 4 == 0 && F_KINV % 4 == 0,
+static_assert(F_HMAX % 4 == 0 && F_GMAX % 4 == 0 && F_QSUM % 4 == 0 && F_KINV % 4 == 0 && F_FINL % 4 == 0 &&
+                  F_FINY % 4 == 0,
               "float4 alignment of the scratch tables");
 
 // ---- TMEM columns ---------------------------------------------------------------------------
@@ -647,7 +648,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       v[0] += __shfl_xor_sync(0xFFFFFFFFu, v[0], 1);
       const int idx = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
-      if ((lane & 1) == 0) F[F_FINY + (q4 * NG + (idx >> 2)) * H + 4 * k + (idx & 3)] = v[0];
+      if ((lane & 1) == 0) F[F_FINY + ((idx >> 2) * H + 4 * k + (idx & 3)) * 4 + q4] = v[0];
       float l[4] = {lsum[0], lsum[1], lsum[2], lsum[3]};
 #pragma unroll
       for (int half = 2, o = 16; half >= 1; half >>= 1, o >>= 1) {
@@ -660,15 +661,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
 #pragma unroll
       for (int o = 4; o >= 1; o >>= 1) l[0] += __shfl_xor_sync(0xFFFFFFFFu, l[0], o);
-      if ((lane & 7) == 0) F[F_FINL + q4 * H + 4 * k + ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1)] = l[0];
+      if ((lane & 7) == 0) F[F_FINL + (4 * k + ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1)) * 4 + q4] = l[0];
     }
     named_bar_sync(3, TOK_THREADS);
     float lt[4];  // sum P over the split per head 4k + j
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      lt[j] = 0.f;
-#pragma unroll
-      for (int w = 0; w < 4; ++w) lt[j] += F[F_FINL + w * H + 4 * k + j];
+      const float4 q = *reinterpret_cast<const float4*>(F + F_FINL + (4 * k + j) * 4);
+      lt[j] = ((0.f + q.x) + q.y + q.z) + q.w;  // quarter order 0..3, as the scalar sum
     }
     float m_ref[4], E[NG];
 #pragma unroll
@@ -688,9 +688,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     const float rs = ((t >> 2) & 1) ? 128.f : 512.f;  // 2^9 / (1 or 4): the element's code weight
     float il[4], ie[NG];  // 1 / sum P per head (0 for an empty split), 1 / E_g (exact: powers of two)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) il[j] = lt[j] > 0.f ? 1.f / lt[j] : 0.f;
+    for (int j = 0; j < 4; ++j) il[j] = lt[j] > 0.f ? __frcp_rn(lt[j]) : 0.f;
 #pragma unroll
-    for (int g = 0; g < NG; ++g) ie[g] = 1.f / E[g];
+    for (int g = 0; g < NG; ++g) ie[g] = __int_as_float((254 << 23) - __float_as_int(E[g]));  // 2^-e for E = 2^e
     float* po = a.part_o + (static_cast<int64_t>(b) * H * S + split) * D + kperm(t);
     const int hs = S * D;  // head stride of part_o
 #pragma unroll
@@ -701,9 +701,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       reg_fence(v);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        float yy = 0.f;
-#pragma unroll
-        for (int w = 0; w < 4; ++w) yy += F[F_FINY + (w * NG + g) * H + 4 * k + j];
+        const float4 q = *reinterpret_cast<const float4*>(F + F_FINY + (g * H + 4 * k + j) * 4);
+        const float yy = ((0.f + q.x) + q.y + q.z) + q.w;
         const float dh = fmaf(__uint_as_float(v[4 + j]), 0.0625f, __uint_as_float(v[j]));
         po[(4 * k + j) * hs + 128 * g] = (dh * rs - yy) * (il[j] * ie[g]);
       }
