@@ -267,6 +267,11 @@ __device__ __forceinline__ void reg_fence(uint32_t (&r)[N]) {
 }
 
 // Bulk prefetch of [p, p + bytes) into L2 (p and bytes 16-byte aligned).
+// Pull the line holding `p` into L2 (no registers, nothing waits on it).
+__device__ __forceinline__ void prefetch_line_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }

@@ -134,6 +134,189 @@ __device__ __noinline__ void exact_code_words(uint32_t taddr, float mean, float 
   }
 }
 
+// The epilogue of one (row, group) of an accumulator: the thread's TMEM lane holds the row's
+// 128 rotated values of the group at columns taddr .. taddr + 127.  kPlain: the rotated row
+// (FP32 and / or BF16).  Otherwise the codec (mean, population variance, Lloyd codes from
+// exact bounds), the packed codes and (scale, zero) by slot, the group's share of the k_pe
+// copy, once per row (group 0) the slot <-> ring maps; window rows also go to the BF16 ring.
+template <bool kPlain>
+__device__ __forceinline__ void epilogue_row_group(const WriterArgs& args, uint32_t taddr, int64_t row, bool valid,
+                                                   int group, int d) {
+  uint32_t r[32];
+
+  if constexpr (kPlain) {
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+      reg_fence(r);
+      if (valid) {
+        const int64_t col = group * 128 + c * 32;
+        if (args.out_f32) {
+          float4* dst = reinterpret_cast<float4*>(args.out_f32 + row * args.ld_out + col);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                 __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+        }
+        if (args.out_bf16) {
+          uint4* dst = reinterpret_cast<uint4*>(args.out_bf16 + row * args.ld_out + col);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            dst[j] = make_uint4(pack_bf16x2(__uint_as_float(r[8 * j]), __uint_as_float(r[8 * j + 1])),
+                                pack_bf16x2(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3])),
+                                pack_bf16x2(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5])),
+                                pack_bf16x2(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7])));
+        }
+      }
+    }
+  } else {
+    // pass 1: mean
+    GroupSum acc;
+    acc.zero();
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+      reg_fence(r);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) acc.add(j & 7, __uint_as_float(r[j]));
+    }
+    const float mean = __fmul_rn(acc.total(), 1.0f / 128.0f);
+    // pass 2: population variance of the centred values
+    acc.zero();
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+      reg_fence(r);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float df = __fsub_rn(__uint_as_float(r[j]), mean);
+        acc.add(j & 7, __fmul_rn(df, df));
+      }
+    }
+    const float var = __fmul_rn(acc.total(), 1.0f / 128.0f);
+    const float stdv = __fsqrt_rn(__fadd_rn(var, 1e-8f));
+    const float thr = args.codec.threshold;
+    // pass 3: codes.  n = RN(diff / std) never decreases as diff grows, so each of the
+    // reference's tests [n >= -t], [n >= 0], [n >= t] is diff >= an exact FP32 bound
+    // found once per (row, group) (FP64 midpoint products; the middle one in closed
+    // form), and diff = RN(x - mean) >= b is x >= X(b): three compares on the raw value
+    // per element.  A std of 2^24 or more, or a search that does not settle, takes the
+    // per-element quotient instead.
+    float b_lo = 0.f, b_mid = 0.f, b_hi = 0.f;
+    bool exact_all = !(stdv < 16777216.f);
+    if (!exact_all) {
+      b_mid = quotient_bound_zero(stdv);
+      b_lo = quotient_bound(-thr, stdv);
+      b_hi = quotient_bound(thr, stdv);
+    }
+    float x_lo = 0.f, x_mid = 0.f, x_hi = 0.f;
+    if (!exact_all)
+      exact_all = !(sub_bound(b_lo, mean, &x_lo) && sub_bound(b_mid, mean, &x_mid) &&
+                    sub_bound(b_hi, mean, &x_hi));
+    uint32_t words[8];
+    if (__any_sync(0xFFFFFFFFu, exact_all)) {
+      exact_code_words(taddr, mean, stdv, thr, words);  // rare: the whole warp, quotient per element
+    } else {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        tmem_ld32(taddr + c * 32, r);
+        tmem_wait_ld();
+        reg_fence(r);
+        uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float x = __uint_as_float(r[j]);
+          const int ncode = set_ge(x, x_lo) + set_ge(x, x_mid) + set_ge(x, x_hi);  // -code
+          if (j < 16)
+            w0 -= static_cast<uint32_t>(ncode) << (2 * j);
+          else
+            w1 -= static_cast<uint32_t>(ncode) << (2 * (j - 16));
+        }
+        words[2 * c] = w0;
+        words[2 * c + 1] = w1;
+      }
+    }
+    const float scale = __fmul_rn(args.codec.scale_factor, stdv);
+    const float zero = __fsub_rn(args.codec.zero_const, __fdiv_rn(mean, scale));
+    RowMeta m{0, -1, false};
+    if (valid) m = row_meta(args, row, args.slots[row]);
+    if (valid && !m.ok && group == 0) report(args.err, ROLAQ_DEV_BAD_SLOT);
+    if (valid && m.ok) {
+      uint4* cdst = reinterpret_cast<uint4*>(args.cache.codes + m.slot * (d / 4) + group * 32);
+      cdst[0] = make_uint4(words[0], words[1], words[2], words[3]);
+      cdst[1] = make_uint4(words[4], words[5], words[6], words[7]);
+      float2* pdst = reinterpret_cast<float2*>(args.cache.params + (m.slot * (d / 128) + group) * 2);
+      *pdst = make_float2(scale, zero);
+      if (args.k_pe != nullptr && m.slot > 0) {
+        // k_pe: each group's epilogue copies its share of the row (all loads before the
+        // stores), so that no group's CTAs carry the whole copy
+        const int dr = args.cache.rope_dim, share = dr / (d / kTileN);
+        const int j0 = (share % 8 == 0 && share <= 32) ? group * (share / 8) : (group == 0 ? 0 : dr / 8);
+        const int j1 = (share % 8 == 0 && share <= 32) ? j0 + share / 8 : dr / 8;
+        const uint4* src = reinterpret_cast<const uint4*>(args.k_pe + row * args.ld_pe);
+        uint4* dst = reinterpret_cast<uint4*>(args.cache.rope + m.slot * dr);
+        for (int j = j0; j < j1; j += 4) {
+          uint4 v[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (j + u < j1) v[u] = src[j + u];
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (j + u < j1) dst[j + u] = v[u];
+        }
+      }
+      if (group == 0 && m.slot > 0) {
+        // the slot <-> ring maps, once per row
+        if (args.cache.rows != nullptr && args.seq_lens != nullptr && args.req_idx != nullptr) {
+          args.cache.rows[m.slot] = static_cast<int32_t>(m.ring);
+          if (m.ring >= 0) args.cache.owners[m.ring] = static_cast<int32_t>(m.slot);
+        }
+      }
+    }
+    // Window rows: BF16 rotated latent into the ring.  The TMEM loads are
+    // warp-collective, so the whole warp reloads when any lane needs it.
+    if (__any_sync(0xFFFFFFFFu, m.ring >= 0)) {
+      uint4* hdst = m.ring >= 0 ? reinterpret_cast<uint4*>(args.cache.hp + m.ring * d + group * 128) : nullptr;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        tmem_ld32(taddr + c * 32, r);
+        tmem_wait_ld();
+        reg_fence(r);
+        if (hdst != nullptr) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            hdst[c * 4 + j] =
+                make_uint4(pack_bf16x2(__uint_as_float(r[8 * j]), __uint_as_float(r[8 * j + 1])),
+                           pack_bf16x2(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3])),
+                           pack_bf16x2(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5])),
+                           pack_bf16x2(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7])));
+        }
+      }
+    }
+  }
+}
+
+// Issued before an epilogue waits for its accumulator: the row's slot, metadata and k_pe
+// share into L2, so that the loads after the codec find them there.
+template <bool kPlain>
+__device__ __forceinline__ void epilogue_prefetch(const WriterArgs& args, int64_t row, int group, int d) {
+  if constexpr (!kPlain) {
+    if (row >= args.n) return;
+    prefetch_line_l2(args.slots + row);
+    if (args.seq_lens != nullptr)
+      prefetch_line_l2(static_cast<const char*>(args.seq_lens) + row * (args.seq_is64 ? 8 : 4));
+    if (args.req_idx != nullptr)
+      prefetch_line_l2(static_cast<const char*>(args.req_idx) + row * (args.req_is64 ? 8 : 4));
+    if (args.positions != nullptr)
+      prefetch_line_l2(static_cast<const char*>(args.positions) + row * (args.pos_is64 ? 8 : 4));
+    if (args.k_pe != nullptr)
+      prefetch_line_l2(args.k_pe + row * args.ld_pe + group * (args.cache.rope_dim / (d / kTileN)));
+  }
+}
+
 template <bool kPlain>
 __global__ void __launch_bounds__(kWriterThreads, 1)
     writer_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
@@ -273,158 +456,17 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
     for (int64_t rt = cg + set * ctas_g; rt < row_tiles; rt += kNumBuf * ctas_g, lt += kNumBuf) {
       const int buf = static_cast<int>(lt % kNumBuf);
       const uint32_t use = static_cast<uint32_t>(lt / kNumBuf);
+      const int64_t row = rt * kTileM + quad * 32 + lane;
+      epilogue_prefetch<kPlain>(args, row, group, d);
       if (!mbar_wait(&tfull[buf], use & 1u, args.err)) {
         *abort_flag = 1;
         break;
       }
       tc_fence_after();
-      const int64_t row = rt * kTileM + quad * 32 + lane;
       const bool valid = row < args.n;
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(buf * kTileN);
-      uint32_t r[32];
-
-      if constexpr (kPlain) {
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld32(taddr + c * 32, r);
-          tmem_wait_ld();
-          reg_fence(r);
-          if (valid) {
-            const int64_t col = group * 128 + c * 32;
-            if (args.out_f32) {
-              float4* dst = reinterpret_cast<float4*>(args.out_f32 + row * args.ld_out + col);
-#pragma unroll
-              for (int j = 0; j < 8; ++j)
-                dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                     __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-            }
-            if (args.out_bf16) {
-              uint4* dst = reinterpret_cast<uint4*>(args.out_bf16 + row * args.ld_out + col);
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                dst[j] = make_uint4(pack_bf16x2(__uint_as_float(r[8 * j]), __uint_as_float(r[8 * j + 1])),
-                                    pack_bf16x2(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3])),
-                                    pack_bf16x2(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5])),
-                                    pack_bf16x2(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7])));
-            }
-          }
-        }
-      } else {
-        // pass 1: mean
-        GroupSum acc;
-        acc.zero();
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld32(taddr + c * 32, r);
-          tmem_wait_ld();
-          reg_fence(r);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) acc.add(j & 7, __uint_as_float(r[j]));
-        }
-        const float mean = __fmul_rn(acc.total(), 1.0f / 128.0f);
-        // pass 2: population variance of the centred values
-        acc.zero();
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld32(taddr + c * 32, r);
-          tmem_wait_ld();
-          reg_fence(r);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float df = __fsub_rn(__uint_as_float(r[j]), mean);
-            acc.add(j & 7, __fmul_rn(df, df));
-          }
-        }
-        const float var = __fmul_rn(acc.total(), 1.0f / 128.0f);
-        const float stdv = __fsqrt_rn(__fadd_rn(var, 1e-8f));
-        const float thr = args.codec.threshold;
-        // pass 3: codes.  n = RN(diff / std) never decreases as diff grows, so each of the
-        // reference's tests [n >= -t], [n >= 0], [n >= t] is diff >= an exact FP32 bound
-        // found once per (row, group) (FP64 midpoint products; the middle one in closed
-        // form), and diff = RN(x - mean) >= b is x >= X(b): three compares on the raw value
-        // per element.  A std of 2^24 or more, or a search that does not settle, takes the
-        // per-element quotient instead.
-        float b_lo = 0.f, b_mid = 0.f, b_hi = 0.f;
-        bool exact_all = !(stdv < 16777216.f);
-        if (!exact_all) {
-          b_mid = quotient_bound_zero(stdv);
-          b_lo = quotient_bound(-thr, stdv);
-          b_hi = quotient_bound(thr, stdv);
-        }
-        float x_lo = 0.f, x_mid = 0.f, x_hi = 0.f;
-        if (!exact_all)
-          exact_all = !(sub_bound(b_lo, mean, &x_lo) && sub_bound(b_mid, mean, &x_mid) &&
-                        sub_bound(b_hi, mean, &x_hi));
-        uint32_t words[8];
-        if (__any_sync(0xFFFFFFFFu, exact_all)) {
-          exact_code_words(taddr, mean, stdv, thr, words);  // rare: the whole warp, quotient per element
-        } else {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            tmem_ld32(taddr + c * 32, r);
-            tmem_wait_ld();
-            reg_fence(r);
-            uint32_t w0 = 0, w1 = 0;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float x = __uint_as_float(r[j]);
-              const int ncode = set_ge(x, x_lo) + set_ge(x, x_mid) + set_ge(x, x_hi);  // -code
-              if (j < 16)
-                w0 -= static_cast<uint32_t>(ncode) << (2 * j);
-              else
-                w1 -= static_cast<uint32_t>(ncode) << (2 * (j - 16));
-            }
-            words[2 * c] = w0;
-            words[2 * c + 1] = w1;
-          }
-        }
-        const float scale = __fmul_rn(args.codec.scale_factor, stdv);
-        const float zero = __fsub_rn(args.codec.zero_const, __fdiv_rn(mean, scale));
-        RowMeta m{0, -1, false};
-        if (valid) m = row_meta(args, row, args.slots[row]);
-        if (valid && !m.ok && group == 0) report(args.err, ROLAQ_DEV_BAD_SLOT);
-        if (valid && m.ok) {
-          uint4* cdst = reinterpret_cast<uint4*>(args.cache.codes + m.slot * (d / 4) + group * 32);
-          cdst[0] = make_uint4(words[0], words[1], words[2], words[3]);
-          cdst[1] = make_uint4(words[4], words[5], words[6], words[7]);
-          float2* pdst = reinterpret_cast<float2*>(args.cache.params + (m.slot * (d / 128) + group) * 2);
-          *pdst = make_float2(scale, zero);
-          if (group == 0 && m.slot > 0) {
-            // k_pe and the slot <-> ring maps, once per row
-            if (args.k_pe != nullptr) {
-              const int dr = args.cache.rope_dim;
-              const uint4* src = reinterpret_cast<const uint4*>(args.k_pe + row * args.ld_pe);
-              uint4* dst = reinterpret_cast<uint4*>(args.cache.rope + m.slot * dr);
-              for (int j = 0; j < dr / 8; ++j) dst[j] = src[j];
-            }
-            if (args.cache.rows != nullptr && args.seq_lens != nullptr && args.req_idx != nullptr) {
-              args.cache.rows[m.slot] = static_cast<int32_t>(m.ring);
-              if (m.ring >= 0) args.cache.owners[m.ring] = static_cast<int32_t>(m.slot);
-            }
-          }
-        }
-        // Window rows: BF16 rotated latent into the ring.  The TMEM loads are
-        // warp-collective, so the whole warp reloads when any lane needs it.
-        if (__any_sync(0xFFFFFFFFu, m.ring >= 0)) {
-          uint4* hdst = m.ring >= 0 ? reinterpret_cast<uint4*>(args.cache.hp + m.ring * d + group * 128) : nullptr;
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            tmem_ld32(taddr + c * 32, r);
-            tmem_wait_ld();
-            reg_fence(r);
-            if (hdst != nullptr) {
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                hdst[c * 4 + j] =
-                    make_uint4(pack_bf16x2(__uint_as_float(r[8 * j]), __uint_as_float(r[8 * j + 1])),
-                               pack_bf16x2(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3])),
-                               pack_bf16x2(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5])),
-                               pack_bf16x2(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7])));
-            }
-          }
-        }
-      }
+      epilogue_row_group<kPlain>(args, taddr, row, valid, group, d);
       tc_fence_before();
       mbar_arrive(&tempty[buf]);
     }
@@ -437,7 +479,6 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
     tmem_dealloc(tmem_base, kTmemCols);
   }
 }
-
 
 // ---- small batches (decode writes): SIMT rotation + codec -------------------------------
 //
@@ -642,7 +683,8 @@ int launch_writer(const uint16_t* x, int64_t ldx, const uint16_t* w, const Write
   rc = make_map_2d(&mw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, static_cast<uint64_t>(d), static_cast<uint64_t>(d),
                    static_cast<uint64_t>(d) * 2, kTileK, kTileN);
   if (rc != ROLAQ_OK) return rc;
-  const int64_t tiles = ((args.n + kTileM - 1) / kTileM) * (d / kTileN);
+  const int groups = d / kTileN;
+  const int64_t tiles = ((args.n + kTileM - 1) / kTileM) * groups;
   const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
   // The attribute is set once per process (and per kernel), not on every launch, so
   // that launches can be captured into CUDA graphs without extra API calls.
