@@ -817,6 +817,7 @@ __global__ void merge_kernel(const float* __restrict__ part_o, int64_t row_strid
 // split; the weights reach the other lanes by shuffle) and merges the partials.
 constexpr int kMwHeads = 4;
 constexpr int kMwThreads = 256;
+constexpr int kMwFastSplits = 12;  // up to this many INT2 splits, phase 2 issues all loads at once
 
 template <int D, int DR>
 __device__ __forceinline__ void window_elems4(const DecodeArgs& a, int64_t slot, int64_t r, int e0, float (&v)[4]) {
@@ -855,7 +856,7 @@ __device__ __forceinline__ void window_elems8(const DecodeArgs& a, int64_t slot,
 }
 
 template <int D, int DR>
-__global__ void __launch_bounds__(kMwThreads) merge_window_kernel(const DecodeArgs a, int heads,
+__global__ void __launch_bounds__(kMwThreads, 2) merge_window_kernel(const DecodeArgs a, int heads,
                                                                   uint16_t* __restrict__ out, int64_t out_sb,
                                                                   int64_t out_sh, float* __restrict__ out_lse) {
   static_assert(D == 4 * 128 && DR == 64, "four latent elements per lane, 16 rope lanes; 8 elements per thread");
@@ -1022,6 +1023,54 @@ __global__ void __launch_bounds__(kMwThreads) merge_window_kernel(const DecodeAr
   grid_dependency_wait();
   const int ns = a.num_splits;
   const float* lse_row = a.part_lse + row * S;
+  uint16_t* const orow = out + b * out_sb + (h0 + hh) * out_sh + j;  // 8-byte aligned rows
+  if (ns <= kMwFastSplits) {
+    // Every split's LSE and partial loaded before any is used (one round trip to L2); the
+    // same operations in the same order as the general loop below.
+    const float lv = lane < ns ? lse_row[lane] : -INFINITY;
+    float4 v[kMwFastSplits][2];
+#pragma unroll
+    for (int p = 0; p < kMwFastSplits; ++p) {
+      if (p < ns) {
+        const float4* src = reinterpret_cast<const float4*>(prow + static_cast<int64_t>(p) * D + j);
+        v[p][0] = src[0];
+        v[p][1] = src[1];
+      }
+    }
+    float m = fmaxf(lse_w, lv);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    const float mref = m == -INFINITY ? 0.f : m;
+    const float ww = lse_w == -INFINITY ? 0.f : __expf(lse_w - mref);
+    float acc[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[c] = ww * ow[c];
+    const float wl = lane < ns ? __expf(lv - mref) : 0.f;  // weight of split lane
+    float den = wl;
+#pragma unroll
+    for (int p = 0; p < kMwFastSplits; ++p) {
+      if (p < ns) {  // uniform across the warp
+        const float w = __shfl_sync(0xFFFFFFFFu, wl, p);
+        const float vv[8] = {v[p][0].x, v[p][0].y, v[p][0].z, v[p][0].w, v[p][1].x, v[p][1].y, v[p][1].z, v[p][1].w};
+#pragma unroll
+        for (int c = 0; c < 8; ++c) acc[c] = w > 0.f ? fmaf(w, vv[c], acc[c]) : acc[c];
+      }
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) den += __shfl_xor_sync(0xFFFFFFFFu, den, o);
+    den += ww;
+    const float inv = den > 0.f ? 1.f / den : 0.f;
+    uint32_t pk[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const __nv_bfloat162 v2 = __floats2bfloat162_rn(acc[2 * c] * inv, acc[2 * c + 1] * inv);
+      pk[c] = *reinterpret_cast<const uint32_t*>(&v2);
+    }
+    reinterpret_cast<uint2*>(orow)[0] = make_uint2(pk[0], pk[1]);
+    reinterpret_cast<uint2*>(orow)[1] = make_uint2(pk[2], pk[3]);
+    if ((tid & 63) == 0 && out_lse) out_lse[row] = den > 0.f ? mref + logf(den) : -INFINITY;
+    return;
+  }
   float m = lse_w;
   for (int p = lane; p < ns; p += 32) m = fmaxf(m, lse_row[p]);
 #pragma unroll
@@ -1066,9 +1115,8 @@ __global__ void __launch_bounds__(kMwThreads) merge_window_kernel(const DecodeAr
     const __nv_bfloat162 v2 = __floats2bfloat162_rn(acc[2 * c] * inv, acc[2 * c + 1] * inv);
     pk[c] = *reinterpret_cast<const uint32_t*>(&v2);
   }
-  uint2* o2 = reinterpret_cast<uint2*>(out + b * out_sb + (h0 + hh) * out_sh + j);  // 8-byte aligned rows
-  o2[0] = make_uint2(pk[0], pk[1]);
-  o2[1] = make_uint2(pk[2], pk[3]);
+  reinterpret_cast<uint2*>(orow)[0] = make_uint2(pk[0], pk[1]);
+  reinterpret_cast<uint2*>(orow)[1] = make_uint2(pk[2], pk[3]);
   if ((tid & 63) == 0 && out_lse) out_lse[row] = den > 0.f ? mref + logf(den) : -INFINITY;
 }
 
