@@ -157,9 +157,12 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   const int first_page = lo / PAGE;
   const int npages = hi > lo ? (hi - 1) / PAGE - first_page + 1 : 0;
-  const int pps = 2 * ((npages + 2 * a.num_splits - 1) / (2 * a.num_splits));
-  const int p0 = first_page + split * pps;
-  const int p1 = min(first_page + npages, p0 + pps);
+  // The range's 128-token tiles (page pairs) spread over the splits as evenly as they go:
+  // the first (tiles % num_splits) splits take one tile more.
+  const int all_tiles = (npages + 1) / 2;
+  const int tbase = all_tiles / a.num_splits, textra = all_tiles % a.num_splits;
+  const int p0 = first_page + 2 * (split * tbase + min(split, textra));
+  const int p1 = min(first_page + npages, p0 + 2 * (tbase + (split < textra ? 1 : 0)));
   if (p0 >= p1) {
     for (int u = tid; u < H * D; u += blockDim.x) {
       const int h = u / D, j = u % D;
