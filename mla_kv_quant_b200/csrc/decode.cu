@@ -809,9 +809,12 @@ __global__ void merge_kernel(const float* __restrict__ part_o, int64_t row_strid
 //
 // Phase 1 does not read the INT2 partials, so it runs while the tcgen05 kernel drains (this
 // kernel is launched as its programmatic dependent): the window rows' slots and ring rows
-// once per CTA; scores with a warp pair per head (warp 2h + e takes rows e, e + 2, ..; lane l
-// owns latent elements 4l + 128u + c and rope elements 4l + c); the window softmax (a warp
-// per head); the window partial (thread: head tid / 64, elements 8 (tid % 64) ..+8), stored
+// once per CTA; the rows staged in shared memory as FP32 with every load issued before any
+// is used (the phase then costs a few round trips to memory, so that it finishes on the SMs
+// the draining grid frees); scores with a warp pair per head (warp 2h + e takes rows e,
+// e + 2, ..; lane l owns latent elements 4l + 128u + c and rope elements 4l + c); the window
+// softmax (a warp per head); the window partial (thread: head tid / 64, elements
+// 8 (tid % 64) ..+8), stored
 // as split num_splits of part_o / part_lse so that the scratch holds every partial after the
 // call.  Phase 2, after griddepcontrol.wait: each warp reads its head's split LSEs (lane =
 // split; the weights reach the other lanes by shuffle) and merges the partials.
@@ -835,26 +838,6 @@ __device__ __forceinline__ void window_elems4(const DecodeArgs& a, int64_t slot,
   }
 }
 
-// Elements e0 .. e0 + 7 of a window row: the BF16 ring row r, or (r < 0: the ring row no
-// longer belongs to the slot) the slot's INT2 codes dequantised as (code - zero) * scale.
-template <int D, int DR>
-__device__ __forceinline__ void window_elems8(const DecodeArgs& a, int64_t slot, int64_t r, int e0, float (&v)[8]) {
-  if (r >= 0) {
-    const uint4 w = *reinterpret_cast<const uint4*>(a.cache.hp + r * D + e0);
-    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      v[2 * c] = __uint_as_float(ws[c] << 16);
-      v[2 * c + 1] = __uint_as_float(ws[c] & 0xFFFF0000u);
-    }
-  } else {
-    const uint32_t cb = *reinterpret_cast<const uint16_t*>(a.cache.codes + slot * (D / 4) + e0 / 4);
-    const float2 sz = reinterpret_cast<const float2*>(a.cache.params)[slot * (D / 128) + e0 / 128];
-#pragma unroll
-    for (int c = 0; c < 8; ++c) v[c] = __fmul_rn(__fsub_rn(static_cast<float>((cb >> (2 * c)) & 3u), sz.y), sz.x);
-  }
-}
-
 template <int D, int DR>
 __global__ void __launch_bounds__(kMwThreads, 2) merge_window_kernel(const DecodeArgs a, int heads,
                                                                   uint16_t* __restrict__ out, int64_t out_sb,
@@ -864,6 +847,8 @@ __global__ void __launch_bounds__(kMwThreads, 2) merge_window_kernel(const Decod
   __shared__ float sc[kMwHeads][kMaxWindow];
   __shared__ int64_t rslot[kMaxWindow], rrow[kMaxWindow];
   __shared__ float stat[kMwHeads][2];  // window lse, window sum of exp
+  extern __shared__ float4 wrow_raw[];
+  float* wrow = reinterpret_cast<float*>(wrow_raw);  // [nw][D + DR] FP32 window rows
   const int hgroups = heads / kMwHeads;
   const int b = blockIdx.x / hgroups, h0 = (blockIdx.x % hgroups) * kMwHeads;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -897,6 +882,46 @@ __global__ void __launch_bounds__(kMwThreads, 2) merge_window_kernel(const Decod
     rslot[tid] = slot;
     rrow[tid] = r;
   }
+  __syncthreads();
+  // The window rows into shared memory as FP32, (D + DR) values per row: every load of the
+  // CTA is issued before any is used.  Latent elements come from the BF16 ring row, or (the
+  // ring row no longer belongs to the slot) from the INT2 codes as (code - zero) * scale;
+  // rope elements from k_pe; a row whose page is out of range stays zero.
+  constexpr int kChunks = (D + DR) / 4;  // 4 values per chunk
+  constexpr int kPerThread = (kMaxWindow * kChunks + kMwThreads - 1) / kMwThreads;
+  {
+    uint2 raw[kPerThread];
+#pragma unroll
+    for (int k = 0; k < kPerThread; ++k) {
+      const int idx = tid + k * kMwThreads;
+      raw[k] = make_uint2(0, 0);
+      if (idx < nw * kChunks) {
+        const int p = idx / kChunks, e4 = 4 * (idx % kChunks);
+        const int64_t slot = rslot[p], r = rrow[p];
+        if (slot >= 0 && e4 >= D)
+          raw[k] = *reinterpret_cast<const uint2*>(a.cache.rope + slot * DR + (e4 - D));
+        else if (slot >= 0 && r >= 0)
+          raw[k] = *reinterpret_cast<const uint2*>(a.cache.hp + r * D + e4);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kPerThread; ++k) {
+      const int idx = tid + k * kMwThreads;
+      if (idx < nw * kChunks) {
+        const int p = idx / kChunks, e4 = 4 * (idx % kChunks);
+        float v[4];
+        if (rslot[p] >= 0 && e4 < D && rrow[p] < 0) {
+          window_elems4<D, DR>(a, rslot[p], -1, e4, v);
+        } else {
+          v[0] = __uint_as_float(raw[k].x << 16);
+          v[1] = __uint_as_float(raw[k].x & 0xFFFF0000u);
+          v[2] = __uint_as_float(raw[k].y << 16);
+          v[3] = __uint_as_float(raw[k].y & 0xFFFF0000u);
+        }
+        *reinterpret_cast<float4*>(wrow + p * (D + DR) + e4) = make_float4(v[0], v[1], v[2], v[3]);
+      }
+    }
+  }
   // the query of head h0 + hw at the lane's elements
   const int hw = warp >> 1, par = warp & 1;
   const uint16_t* qh = a.q + b * a.q_sb + (h0 + hw) * a.q_sh;
@@ -917,52 +942,28 @@ __global__ void __launch_bounds__(kMwThreads, 2) merge_window_kernel(const Decod
     qr[3] = __uint_as_float(w.y & 0xFFFF0000u);
   }
   __syncthreads();
-  // scores: rows p = par + 2 i; the loads of four rows are issued before any of them is used
-  for (int i0 = 0; i0 < kMaxWindow / 2 && par + 2 * i0 < nw; i0 += 4) {
-    uint2 hv[4][4], rv[4];
-    bool ring[4];
+  // scores: a warp pair per head, rows p = par + 2 i, from shared memory
+  for (int p = par; p < nw; p += 2) {
+    float acc = 0.f;
+    if (rslot[p] >= 0) {
+      const float* wr = wrow + p * (D + DR);
 #pragma unroll
-    for (int ii = 0; ii < 4; ++ii) {
-      const int p = par + 2 * (i0 + ii);
-      const int64_t slot = p < nw ? rslot[p] : -1, r = p < nw ? rrow[p] : -1;
-      ring[ii] = slot >= 0 && r >= 0;
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        hv[ii][u] = ring[ii] ? *reinterpret_cast<const uint2*>(a.cache.hp + r * D + 4 * lane + 128 * u)
-                             : make_uint2(0, 0);
-      rv[ii] = (slot >= 0 && lane < DR / 4) ? *reinterpret_cast<const uint2*>(a.cache.rope + slot * DR + 4 * lane)
-                                           : make_uint2(0, 0);
-    }
-#pragma unroll
-    for (int ii = 0; ii < 4; ++ii) {
-      const int p = par + 2 * (i0 + ii);
-      if (p >= nw) break;  // uniform across the warp
-      const int64_t slot = rslot[p];
-      float acc = 0.f;
-      if (slot >= 0) {
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          float v[4];
-          if (ring[ii]) {
-            v[0] = __uint_as_float(hv[ii][u].x << 16);
-            v[1] = __uint_as_float(hv[ii][u].x & 0xFFFF0000u);
-            v[2] = __uint_as_float(hv[ii][u].y << 16);
-            v[3] = __uint_as_float(hv[ii][u].y & 0xFFFF0000u);
-          } else {  // the ring row no longer belongs to the slot: INT2 codes
-            window_elems4<D, DR>(a, slot, -1, 4 * lane + 128 * u, v);
-          }
-#pragma unroll
-          for (int c = 0; c < 4; ++c) acc = fmaf(qv[4 * u + c], v[c], acc);
-        }
-        acc = fmaf(qr[0], __uint_as_float(rv[ii].x << 16), acc);
-        acc = fmaf(qr[1], __uint_as_float(rv[ii].x & 0xFFFF0000u), acc);
-        acc = fmaf(qr[2], __uint_as_float(rv[ii].y << 16), acc);
-        acc = fmaf(qr[3], __uint_as_float(rv[ii].y & 0xFFFF0000u), acc);
+      for (int u = 0; u < 4; ++u) {
+        const float4 v = *reinterpret_cast<const float4*>(wr + 4 * lane + 128 * u);
+        acc = fmaf(qv[4 * u], v.x, acc);
+        acc = fmaf(qv[4 * u + 1], v.y, acc);
+        acc = fmaf(qv[4 * u + 2], v.z, acc);
+        acc = fmaf(qv[4 * u + 3], v.w, acc);
       }
-#pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
-      if (lane == 0) sc[hw][p] = acc * a.sm_scale;
+      const float4 v = lane < DR / 4 ? *reinterpret_cast<const float4*>(wr + D + 4 * lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+      acc = fmaf(qr[0], v.x, acc);
+      acc = fmaf(qr[1], v.y, acc);
+      acc = fmaf(qr[2], v.z, acc);
+      acc = fmaf(qr[3], v.w, acc);
     }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+    if (lane == 0) sc[hw][p] = acc * a.sm_scale;
   }
   __syncthreads();
   if (warp < kMwHeads) {  // window softmax of head h0 + warp
@@ -981,30 +982,26 @@ __global__ void __launch_bounds__(kMwThreads, 2) merge_window_kernel(const Decod
     }
   }
   __syncthreads();
-  // window partial of head hh at elements j .. j + 7 (rows re-read: L1 hits)
+  // window partial of head hh at elements j .. j + 7; rows past nw (up to a multiple of 4)
+  // add 0 * 0
   const int hh = tid >> 6, j = 8 * (tid & 63);
   float ow[8];
 #pragma unroll
   for (int c = 0; c < 8; ++c) ow[c] = 0.f;
-  for (int p0 = 0; p0 < nw; p0 += 4) {  // four rows' loads in flight at once
-    float v[4][8];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int p = p0 + u;
-      const int64_t slot = p < nw ? rslot[p] : -1;
-      if (slot >= 0) {
-        window_elems8<D, DR>(a, slot, rrow[p], j, v[u]);
-      } else {
-#pragma unroll
-        for (int c = 0; c < 8; ++c) v[u][c] = 0.f;
+  const int nw4 = (nw + 3) & ~3;
+  for (int p = 0; p < nw4; ++p) {
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float e = 0.f;
+    if (p < nw) {
+      e = sc[hh][p];
+      if (rslot[p] >= 0) {
+        const float4 v0 = *reinterpret_cast<const float4*>(wrow + p * (D + DR) + j);
+        const float4 v1 = *reinterpret_cast<const float4*>(wrow + p * (D + DR) + j + 4);
+        v[0] = v0.x, v[1] = v0.y, v[2] = v0.z, v[3] = v0.w, v[4] = v1.x, v[5] = v1.y, v[6] = v1.z, v[7] = v1.w;
       }
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const float e = p0 + u < nw ? sc[hh][p0 + u] : 0.f;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) ow[c] = fmaf(e, v[u][c], ow[c]);
-    }
+    for (int c = 0; c < 8; ++c) ow[c] = fmaf(e, v[c], ow[c]);
   }
   const float lse_w = stat[hh][0];
   const float il = nw > 0 ? 1.f / stat[hh][1] : 0.f;
@@ -1215,6 +1212,12 @@ int launch_decode_merged(const DecodeArgs& a, int heads, uint16_t* out, int64_t 
       (reinterpret_cast<uintptr_t>(a.part_o) & 15u))
     return ROLAQ_EUNSUPPORTED;
   if (heads % kMwHeads != 0) return ROLAQ_EUNSUPPORTED;
+  // the merge kernel stages the window rows (at most sink + recent <= kMaxWindow) as FP32
+  constexpr int kMwRowBytes = (512 + 64) * 4;
+  static const bool mw_attr = cudaFuncSetAttribute(merge_window_kernel<512, 64>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   kMaxWindow * kMwRowBytes) == cudaSuccess;
+  if (!mw_attr) return ROLAQ_ECUDA;
   int rc = launch_decode_tc(a, s);
   if (rc != ROLAQ_OK) return rc;
   // Programmatic dependent launch: the window phase overlaps the tcgen05 kernel's last CTAs;
@@ -1222,7 +1225,7 @@ int launch_decode_merged(const DecodeArgs& a, int heads, uint16_t* out, int64_t 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(int64_t(a.batch) * heads / kMwHeads));
   cfg.blockDim = dim3(kMwThreads);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = static_cast<size_t>(max(0, a.cache.sink + a.cache.recent)) * kMwRowBytes;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
