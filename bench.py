@@ -590,15 +590,47 @@ def run_seqsplit(args, rank, world, dev):
             coll.append(ev[1].elapsed_time(ev[2]) * 1e3)
     k_us = sorted(kern)[len(kern) // 2]
     c_us = sorted(coll)[len(coll) // 2]
-    t = torch.tensor([k_us, c_us, k_us + c_us], device=dev)
+
+    # The same layer replayed from a CUDA graph, the NCCL all-gather captured with the decode
+    # and the merge: no host launch gaps between them.
+    def layer_and_merge():
+        layer()
+        if world > 1:
+            gather_merge(o_loc, lse_loc)
+
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        layer_and_merge()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        layer_and_merge()
+    gl = []
+    for it in range(args.warmup + args.steps):
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        ev[0].record()
+        graph.replay()
+        ev[2].record()
+        torch.cuda.synchronize()
+        if it >= args.warmup:
+            gl.append(ev[0].elapsed_time(ev[2]) * 1e3)
+    torch.cuda.synchronize()
+    del graph  # before the process group goes: the graph holds the NCCL call
+    g_us = sorted(gl)[len(gl) // 2]
+    t = torch.tensor([k_us, c_us, k_us + c_us, g_us], device=dev)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     return {"mode": "seqsplit", "n_gpus": world, "batch": 1, "ctx": ctx, "tokens_per_rank": n,
             "num_splits_per_rank": splits, "us_per_layer": float(t[2]), "kernel_us": float(t[0]),
-            "gather_merge_us": float(t[1]),
+            "gather_merge_us": float(t[1]), "us_per_layer_graph": float(t[3]),
             "note": "median over steps of each rank, max over ranks; kernel = the slice's decode call (INT2 "
                     "splits + window + merge to one BF16 partial and its LSE), gather_merge = one NCCL "
-                    "all-gather of the (o, lse) partials + the merge kernel"}
+                    "all-gather of the (o, lse) partials + the merge kernel (eager launches); "
+                    "us_per_layer_graph = the same layer replayed from a CUDA graph"}
 
 
 def main():
