@@ -25,7 +25,6 @@ import datetime
 import json
 import math
 import os
-import re
 import statistics
 import subprocess
 import sys
@@ -45,6 +44,7 @@ LAYERS, HEADS, D, DR = 27, 16, 512, 64
 SINK, RECENT = 4, 16
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
+REF_SAMPLE_REQS = 2  # requests per step of the reference arm (one layer each)
 
 
 def peaks():
@@ -69,12 +69,15 @@ def writer_bytes(rows, d=D, dr=DR):
 
 
 def read_traffic():
-    """Per-launch DRAM bytes of the decode call from the committed ncu summary (or None)."""
-    f = ROOT / "profiles" / "decode_tc_b64_ctx16k.md"
+    """Per-launch DRAM bytes (read + write) of the decode call as one ncu capture measured
+    them, with the capture it came from: ``profiles/decode_traffic.json`` holds the figure
+    and the command next to the markdown summary of the same capture.  (None, None) when
+    the file is absent: no stale constant is reported."""
+    f = ROOT / "profiles" / "decode_traffic.json"
     if not f.exists():
-        return None
-    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read_text())
-    return float(m.group(1)) if m else None
+        return None, None
+    j = json.loads(f.read_text())
+    return float(j["traffic_bytes_per_launch"]), j.get("source")
 
 
 class ClockSampler:
@@ -372,6 +375,7 @@ def run_ours(args, rank, world, dev):
 
     dbytes = decode_bytes(batch, ctx)
     achieved = dbytes / dec_s / 1e9
+    traffic, traffic_src = read_traffic()
     res = {
         "metric": METRIC,
         "value": world * batch / step_s,
@@ -402,7 +406,7 @@ def run_ours(args, rank, world, dev):
                           "path": "the same calls and copies launched eagerly every step"}},
         "roofline": {"kernel": "rolaq decode (decode_tc_kernel + merge_window_kernel), one layer", "bound": "hbm",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_source": f"{peak_kind} hbm_gbs", "traffic": read_traffic(),
+                     "peak_source": f"{peak_kind} hbm_gbs", "traffic": traffic, "traffic_source": traffic_src,
                      "algorithmic_bytes_per_launch": dbytes, "launch_us": dec_s * 1e6},
         "writer": {"rows_per_launch": wrows, "launch_us": w_s * 1e6, "gbs": w_bytes / w_s / 1e9,
                    "hbm_frac": (w_bytes / w_s / 1e9) / hbm, "tflops": w_flops / w_s / 1e12,
@@ -412,8 +416,135 @@ def run_ours(args, rank, world, dev):
                    "note": "roofline_frac = max(bytes/HBM peak, flops/bf16 peak) / time, of " + peak_kind},
         "clocks": clocks,
         "gpu_launches": args.steps * LAYERS * 3,
+        "gpus_active": world,
     }
     return res
+
+
+# Configs 3a / 3b: decode plus writer on 1 x B200.  MiniCPM3-4B's
+# softmax scale is 1/sqrt(qk_nope_head_dim + qk_rope_head_dim) with the model's published
+# head dims 64 + 32 (the checkpoint is not in this container: a stated parameter).
+EXTRA_CONFIGS = {
+    "3a_minicpm3_4b": dict(layers=62, heads=40, d=256, dr=32, batch=128, ctx=8192, sm_scale=1.0 / math.sqrt(96.0)),
+    "3b_moonlight_16b_a3b": dict(layers=27, heads=16, d=512, dr=64, batch=128, ctx=8192,
+                                 sm_scale=1.0 / math.sqrt(192.0)),
+}
+
+
+def decode_step_config(dev, layers, heads, d, dr, batch, ctx, sm_scale, steps, warmup, world=1, seed=0):
+    """One decode step of ``layers`` MLA layers for ``batch`` requests at ``ctx`` tokens (per
+    layer: the fused writer stores the new latents, then the packed decode reads the INT2
+    cache), replayed from a CUDA graph; plus the decode launch alone (CUDA events around
+    each launch, eager) for the roofline.  The cache is filled through the same fused
+    writer (8 requests x ctx rows per launch)."""
+    from mla_kv_quant_b200 import ops, synth
+    from mla_kv_quant_b200.pool import PackedLatentPool
+
+    rot = {i: synth.rotation(d, 1000 + i) for i in range(layers)}
+    params = synth.layer_params(layers, seed=2)
+    pt, num_slots = synth.page_table(batch, ctx, seed=4 + seed, device=dev)
+    pool = PackedLatentPool(num_slots, layers, d, dr, max_reqs=batch, sink=SINK, recent=RECENT, device=dev,
+                            rotations=rot, quantizer_params=params)
+    scale = synth.channel_scale(d, 77, dev)
+    pos = torch.arange(ctx, device=dev)
+    for li in range(layers):
+        rt, codec, view = pool.write_rotation_t(li), pool.codec(li), pool.layer_view(li)
+        for b0 in range(0, batch, 8):
+            bs = list(range(b0, min(batch, b0 + 8)))
+            n = len(bs) * ctx
+            x = synth.latents(n, d, seed + 131 * li + b0, dev, scale=scale)
+            pe = synth.normal_bf16((n, dr), seed + 7 * li + b0 + 1, dev)
+            slots = torch.cat([pt[b, pos // 64].long() * 64 + pos % 64 for b in bs])
+            req = torch.tensor(bs, device=dev).repeat_interleave(ctx)
+            ops.fused_write(x, pe, slots, rt, codec, view, seq_lens=torch.full((n,), ctx, dtype=torch.int32,
+                                                                               device=dev),
+                            req_idx=req, positions=pos.repeat(len(bs)).to(torch.int32))
+            del x, pe, slots, req
+    torch.cuda.synchronize()
+    splits = ops.default_num_splits(batch, ctx, latent_dim=d, rope_dim=dr, heads=heads)
+    q = synth.normal_bf16((layers, batch, heads, d + dr), 11 + seed, dev)
+    new_ckv = synth.latents(layers * batch, d, 12 + seed, dev).view(layers, batch, d)
+    new_pe = synth.normal_bf16((layers, batch, dr), 13 + seed, dev)
+    out = torch.empty(layers, batch, heads, d, dtype=torch.bfloat16, device=dev)
+    seq = torch.full((batch,), ctx, dtype=torch.int32, device=dev)
+    req = torch.arange(batch, device=dev, dtype=torch.int64)
+    loc = (pt[:, (ctx - 1) // 64].long() * 64 + (ctx - 1) % 64).contiguous()
+    part_o = torch.empty(batch, heads, splits + 1, d, device=dev)
+    part_lse = torch.empty(batch, heads, splits + 1, device=dev)
+    views = [pool.layer_view(li) for li in range(layers)]
+    rts = [pool.write_rotation_t(li) for li in range(layers)]
+    codecs = [pool.codec(li) for li in range(layers)]
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(layers)]
+
+    def step(timed=False):
+        for li in range(layers):
+            ops.fused_write(new_ckv[li], new_pe[li], loc, rts[li], codecs[li], views[li], seq_lens=seq, req_idx=req)
+            if timed:
+                ev[li][0].record()
+            ops.packed_decode(q[li], views[li], pt, seq, sm_scale, splits, part_o, part_lse, out[li])
+            if timed:
+                ev[li][1].record()
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    dec = []
+    for _ in range(2):
+        step(timed=True)
+        torch.cuda.synchronize()
+        dec += [a.elapsed_time(b) / 1e3 for a, b in ev]
+    dec_s = statistics.mean(dec)
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(warmup):
+        graph.replay()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(steps):
+        graph.replay()
+    s1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    step_s = max_over_ranks(s0.elapsed_time(s1) / 1e3 / steps, world, dev)
+    del graph
+    hbm = peaks()[0]
+    dbytes = decode_bytes(batch, ctx, heads=heads, d=d, dr=dr)
+    res = {"tok_s": world * batch / step_s, "ms_per_step": step_s * 1e3, "steps": steps, "warmup": warmup,
+           "layers": layers, "heads": heads, "kv_lora_rank": d, "rope_dim": dr, "batch_per_gpu": batch, "ctx": ctx,
+           "sm_scale": sm_scale, "num_splits": splits,
+           "decode_kernel": "decode_tc (tcgen05)" if (d, dr, heads) == (512, 64, 16) else "decode_kernel (warp MMA)",
+           "roofline": {"bound": "hbm", "launch_us": dec_s * 1e6, "algorithmic_bytes_per_launch": dbytes,
+                        "achieved": dbytes / dec_s / 1e9, "peak": hbm, "unit": "GB/s",
+                        "frac": dbytes / dec_s / 1e9 / hbm}}
+    del pool, q, new_ckv, new_pe, out, part_o, part_lse
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_batch4a(args, rank, world, dev):
+    """Config 4(a): 512 requests x 32768 tokens of context, 27 DeepSeek-V2-Lite layers,
+    sharded by request over the ranks (512 / N each, no data-path collective); one GPU
+    holds all 512 (~130 GB of cache).  Strong scaling: value = 512 tokens per step / the
+    step time (max over ranks)."""
+    total = 512
+    if total % world:
+        raise SystemExit("--gpus must divide 512")
+    r = decode_step_config(dev, LAYERS, HEADS, D, DR, total // world, 32768, 1.0 / math.sqrt(192.0),
+                           args.steps, args.warmup, world=world, seed=rank)
+    return {"mode": "batch4a", "metric": "INT2 MLA decode tok/s, B512 x 32K ctx, request-sharded", "n_gpus": world,
+            "gpus_active": world, "value": r["tok_s"], "unit": "tok/s", "scaling": "strong",
+            "global_batch": total, **{k: v for k, v in r.items() if k != "tok_s"}}
 
 
 def max_over_ranks(x, world, dev):
@@ -454,34 +585,130 @@ def cpu_decode_sample(batch_sample=2, ctx=16384, seed=0):
     return dt / batch_sample
 
 
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or "unknown"
+
+
 def cpu_baseline(batch, ctx):
     per = cpu_decode_sample(2, ctx)
     step = per * batch * LAYERS
     return {"value": batch / step, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+            "cpu": cpu_model(),
             "sample": f"oracle.decode (numpy FP32, BLAS on all {os.cpu_count()} host threads): 2 requests x 1 layer "
-                      f"x ctx {ctx}, scaled to {batch} requests x {LAYERS} layers per step"}
+                      f"x ctx {ctx}, i.e. 2/{LAYERS} of a token per request; tok/s = requests / ({LAYERS} x seconds "
+                      "per request-layer)"}
+
+
+def _reference_rotate_quantize():
+    """The reference's own ``mla_quant.quantizer.rotate_quantize`` when the unmodified
+    reference is installed in ``baseline/_ref`` (it travels with the repository copy),
+    else None."""
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "mla_quant" / "quantizer.py").exists():
+        return None, None
+    if str(ref) not in sys.path:
+        sys.path.insert(0, str(ref))
+    try:
+        from mla_quant.numerics import configure_reference_numerics
+        from mla_quant.quantizer import rotate_quantize
+    except Exception:  # noqa: BLE001 -- an unusable install falls back to the port
+        return None, None
+    return rotate_quantize, configure_reference_numerics
+
+
+def cpu_qdq_baseline(reps=10):
+    """Config 0: the reference's PyTorch CPU quantize-dequantize (``rotate_quantize``,
+    ``mla_quant/quantizer.py:102-124``) on one ``[1, 4096, 512]`` BF16 latent with an
+    s4r16 mask, timed on this host at 1 thread and at all threads (median of ``reps``
+    calls after 2 warm-ups).  The reference itself when ``baseline/_ref`` holds it, else
+    the oracle's restatement (``oracle.quantizer``)."""
+    from mla_kv_quant_b200 import synth
+
+    n, d = 4096, 512
+    lat = synth.latents(n, d, seed=0)  # BF16, configs[0] distribution
+    r = synth.rotation(d, seed=1)
+    t = float(torch.empty(1).uniform_(0.7, 1.0, generator=torch.Generator().manual_seed(2)))
+    g = synth.signal_gain(t)
+    mask = torch.zeros(n, dtype=torch.bool)
+    mask[:4] = True
+    mask[-16:] = True
+    ref_fn, configure = _reference_rotate_quantize()
+    if ref_fn is not None:
+        configure()
+        x3 = lat.reshape(1, n, d)
+        tt, gt = torch.tensor(t, dtype=torch.float32), torch.tensor(g, dtype=torch.float32)
+
+        def call():
+            ref_fn(x3, r, 128, "oscar_lloyd", tt, gt, high_precision_mask=mask)
+
+        kind, what = "reference", "mla_quant.quantizer.rotate_quantize from baseline/_ref (unmodified reference)"
+    else:
+        from oracle import quantizer as oquant
+
+        xf, rf, mk = lat.float().numpy(), r.numpy(), mask.numpy()
+
+        def call():
+            oquant.rotate_quantize(xf, rf, t, g, mask=mk)
+
+        kind, what = "port", "oracle.quantizer.rotate_quantize (restatement; the reference is not installed here)"
+    out = {}
+    prev = torch.get_num_threads()
+    for label, threads in (("1_thread", 1), ("all_threads", os.cpu_count() or 1)):
+        torch.set_num_threads(threads)
+        for _ in range(2):
+            call()
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            call()
+            ts.append(time.perf_counter() - t0)
+        sec = statistics.median(ts)
+        out[label] = {"threads": threads, "s_per_call": sec, "tok_s": n / sec,
+                      "gbs": n * (2 * d + 2 * d) / sec / 1e9}
+    torch.set_num_threads(prev)
+    return {"config": "configs[0]: [1, 4096, 512] bf16 latent, R 512x512, s4r16 mask, group 128", "kind": kind,
+            "what": what, "cpu": cpu_model(), "cores": os.cpu_count(), "reps": reps, "statistic": "median",
+            "bytes_per_token": 2 * d + 2 * d, **out}
 
 
 def run_reference(args, rank, world):
+    """The reference arm: the path's CPU implementation on the host cores.  The reference's
+    decode kernel is upstream Triton (not vendored), so the timed code is the oracle's
+    restatement of its math (kind "port").  One *step* of this arm is one bounded sample of
+    the benchmark workload, timed for real: ``REF_SAMPLE_REQS`` requests x 1 layer of the
+    decode at the benchmark context, which is ``REF_SAMPLE_REQS / 27`` of a decode token per
+    request; ``value`` = tokens/s = requests / (27 x seconds per request-layer), the same
+    unit as our arm's.  ``ms_per_step`` is the measured sample time (not an extrapolation),
+    so ``steps x ms_per_step`` is the real timed region."""
     if rank != 0:
         return None
     batch, ctx = args.batch, args.ctx
+    reqs = REF_SAMPLE_REQS
     for _ in range(args.warmup):
-        cpu_decode_sample(1, ctx)
+        cpu_decode_sample(reqs, ctx, seed=1)
     times = []
-    for _ in range(args.steps_ref):
-        times.append(cpu_decode_sample(1, ctx) * batch * LAYERS)
+    for i in range(args.steps):
+        times.append(cpu_decode_sample(reqs, ctx, seed=2 + i) * reqs)  # seconds per sample
     step = statistics.median(times)
-    val = batch / step
+    val = reqs / (LAYERS * step)
     return {
         "metric": METRIC, "impl": "reference", "value": val, "unit": "tok/s", "n_gpus": world,
-        "steps": args.steps_ref, "warmup": args.warmup, "ms_per_step": step * 1e3, "higher_is_better": True,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"decode step: {LAYERS} layers x batch {batch} x ctx {ctx} (sampled: 1 request x "
-                               "1 layer per step, scaled)", "batch_per_gpu": batch, "ctx": ctx,
-                   "parallelism": "host CPU, one process"},
-        "cpu_baseline": {"value": val, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-                         "sample": "oracle.decode (numpy FP32, all host threads), 1 request x 1 layer per step"},
+        "config": {"workload": f"decode step: {LAYERS} layers x batch {batch} x ctx {ctx}; one step of this arm = "
+                               f"{reqs} requests x 1 layer of it (a bounded sample, timed as run)",
+                   "batch_per_gpu": batch, "ctx": ctx, "parallelism": "host CPU, one process"},
+        "cpu_baseline": {"value": val, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port", "cpu": cpu_model(),
+                         "sample": f"oracle.decode (numpy FP32, BLAS on all {os.cpu_count()} host threads), "
+                                   f"{reqs} requests x 1 layer x ctx {ctx} per step"},
         "e2e": {"value": val, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -635,9 +862,10 @@ def run_seqsplit(args, rank, world, dev):
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--mode", choices=["step", "decode-layer", "writer-layer", "seqsplit"], default="step",
+    ap.add_argument("--mode", choices=["step", "decode-layer", "writer-layer", "seqsplit", "batch4a"], default="step",
                     help="step: the benchmark; *-layer: one layer, 3 launches (for ncu captures); "
-                         "seqsplit: one 128K-token request split over the ranks (latency per layer)")
+                         "seqsplit: one 128K-token request split over the ranks (latency per layer); "
+                         "batch4a: 512 requests x 32K sharded over the ranks")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
@@ -645,8 +873,8 @@ def main():
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--ctx", type=int, default=16384)
     ap.add_argument("--splits", type=int, default=0, help="INT2 KV splits per request (0: auto)")
-    ap.add_argument("--steps-ref", type=int, default=3, help="timed samples of the reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra-configs", action="store_true", help="skip the configs 3a / 3b lines")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -660,6 +888,20 @@ def main():
         if world > 1:
             torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
         res = run_seqsplit(args, rank, world, dev)
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+        if rank == 0:
+            print(json.dumps(res))
+        return 0
+    if args.mode == "batch4a":
+        torch.cuda.set_device(local)
+        dev = torch.device("cuda", local)
+        if world > 1:
+            torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+            print(f"rank {rank}/{world} on {torch.cuda.get_device_name(dev)} "
+                  f"({torch.cuda.get_device_properties(dev).uuid})", file=sys.stderr)
+        res = run_batch4a(args, rank, world, dev)
         if world > 1:
             torch.distributed.barrier()
             torch.distributed.destroy_process_group()
@@ -683,9 +925,15 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        print(f"rank {rank}/{world} on {torch.cuda.get_device_name(dev)} "
+              f"({torch.cuda.get_device_properties(dev).uuid})", file=sys.stderr)
     res = run_ours(args, rank, world, dev)
+    if world == 1 and not args.no_extra_configs:
+        res["configs"] = {name: decode_step_config(dev, **cfg, steps=max(3, min(args.steps, 20)), warmup=args.warmup)
+                          for name, cfg in EXTRA_CONFIGS.items()}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline(args.batch, args.ctx)
+        res["cpu_qdq_baseline"] = cpu_qdq_baseline()
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

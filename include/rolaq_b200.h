@@ -61,13 +61,21 @@ typedef struct rolaq_layer_cache {
   int64_t max_reqs;
 } rolaq_layer_cache;
 
-/* Scalars of the learned Lloyd INT2 codec, already rounded to FP32 the way the
- * calling path rounds them (mla_quant/quantizer.py:31-35 for the HF path,
- * deployment/sglang/QuantKernel/mla_fused_writer.py:158-164 for serving). */
+/* Codec families of the INT2 writer. */
+#define ROLAQ_CODEC_LLOYD 0   /* learned Lloyd grid (mla_quant/oscar.py:120-144) */
+#define ROLAQ_CODEC_UNIFORM 1 /* OSCAR's uniform min/max baseline (mla_quant/oscar.py:91-101) */
+
+/* Scalars of the INT2 codec, already rounded to FP32 the way the calling path rounds
+ * them (mla_quant/quantizer.py:31-35 for the HF path,
+ * deployment/sglang/QuantKernel/mla_fused_writer.py:158-164 for serving).
+ * family ROLAQ_CODEC_UNIFORM ignores the three scalars: per 128-group
+ * scale = (max - min) / 3 (1 when |max - min| <= 1e-8), code = clamp(round_half_even(
+ * (x - min) / scale), 0, 3), and the stored zero is FP32(-min / scale). */
 typedef struct rolaq_codec {
   float threshold;    /* t:  code = [n >= -t] + [n >= 0] + [n >= t] */
   float scale_factor; /* FP32((span / 3) * gain); scale = scale_factor * std */
   float zero_const;   /* FP32(-C0 / (span / 3)); zero = zero_const - mean / scale */
+  int32_t family;     /* ROLAQ_CODEC_LLOYD or ROLAQ_CODEC_UNIFORM */
 } rolaq_codec;
 
 /* Library version (major * 10000 + minor * 100 + patch). */

@@ -20,6 +20,9 @@ ROLAQ_EINVAL = -1
 ROLAQ_EUNSUPPORTED = -2
 ROLAQ_ECUDA = -3
 
+CODEC_LLOYD = 0
+CODEC_UNIFORM = 1
+
 DEV_BAD_SLOT = 1
 DEV_BAD_PAGE = 2
 DEV_TIMEOUT = 4
@@ -65,7 +68,12 @@ class LayerCache(ctypes.Structure):
 class Codec(ctypes.Structure):
     """``rolaq_codec``."""
 
-    _fields_ = [("threshold", ctypes.c_float), ("scale_factor", ctypes.c_float), ("zero_const", ctypes.c_float)]
+    _fields_ = [
+        ("threshold", ctypes.c_float),
+        ("scale_factor", ctypes.c_float),
+        ("zero_const", ctypes.c_float),
+        ("family", ctypes.c_int32),
+    ]
 
 
 class RolaqError(RuntimeError):

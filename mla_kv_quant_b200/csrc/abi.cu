@@ -69,6 +69,8 @@ int check_cache(const rolaq_layer_cache* c, bool need_window, bool need_rope = t
 }
 
 int codec_ok(const rolaq_codec& k) {
+  if (k.family == ROLAQ_CODEC_UNIFORM) return ROLAQ_OK;  // no scalars
+  if (k.family != ROLAQ_CODEC_LLOYD) return fail(ROLAQ_EINVAL, "unknown codec family %d", (int)k.family);
   if (!(k.threshold > 0.f) || !(k.scale_factor > 0.f) || !(k.threshold < 1e30f) || !(k.scale_factor < 1e30f))
     return fail(ROLAQ_EINVAL, "codec threshold and scale_factor must be finite and > 0");
   return ROLAQ_OK;

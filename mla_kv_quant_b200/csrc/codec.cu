@@ -25,6 +25,33 @@ __global__ void scatter_pack_kernel(const float* __restrict__ x, int64_t ldx, co
     return;
   }
   const float4* v = reinterpret_cast<const float4*>(x + row * ldx + g * 128);
+  if (codec.family == ROLAQ_CODEC_UNIFORM) {  // OSCAR's uniform min/max codec
+    float mn = INFINITY, mx = -INFINITY;
+    for (int c = 0; c < 32; ++c) {
+      const float4 q = v[c];
+      mn = fminf(fminf(mn, q.x), fminf(fminf(q.y, q.z), q.w));
+      mx = fmaxf(fmaxf(mx, q.x), fmaxf(fmaxf(q.y, q.z), q.w));
+    }
+    const float scale = uniform_scale(mn, mx);
+    uint4* cdst = reinterpret_cast<uint4*>(codes + slot * (d / 4) + g * 32);
+    uint32_t words[8];
+    for (int w = 0; w < 8; ++w) {
+      uint32_t word = 0;
+      for (int j = 0; j < 4; ++j) {
+        const float4 q = v[w * 4 + j];
+        const int b = 8 * j;
+        word |= uniform_code(q.x, mn, scale) << (b + 0);
+        word |= uniform_code(q.y, mn, scale) << (b + 2);
+        word |= uniform_code(q.z, mn, scale) << (b + 4);
+        word |= uniform_code(q.w, mn, scale) << (b + 6);
+      }
+      words[w] = word;
+    }
+    cdst[0] = make_uint4(words[0], words[1], words[2], words[3]);
+    cdst[1] = make_uint4(words[4], words[5], words[6], words[7]);
+    reinterpret_cast<float2*>(params)[slot * ng + g] = make_float2(scale, uniform_zero(mn, scale));
+    return;
+  }
   GroupSum acc;
   acc.zero();
   for (int c = 0; c < 32; ++c) {

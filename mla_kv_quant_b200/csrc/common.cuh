@@ -421,6 +421,21 @@ __device__ __forceinline__ uint32_t lloyd_code(float diff, float std_, float t) 
   return static_cast<uint32_t>(n >= -t) + static_cast<uint32_t>(n >= 0.f) + static_cast<uint32_t>(n >= t);
 }
 
+// OSCAR's uniform min/max INT2 step of one group (mla_quant/oscar.py:91-101): the FP32
+// range divided by 3, or 1 for a (near-)constant group (torch compares |max - min| with
+// the scalar 1e-8 rounded to FP32).
+__device__ __forceinline__ float uniform_scale(float mn, float mx) {
+  const float r = __fsub_rn(mx, mn);
+  return fabsf(r) > 1e-8f ? __fdiv_rn(r, 3.0f) : 1.0f;
+}
+// code = clamp(round((x - min) / scale), 0, 3) with torch.round's ties-to-even (rintf).
+__device__ __forceinline__ uint32_t uniform_code(float x, float mn, float scale) {
+  const float q = rintf(__fdiv_rn(__fsub_rn(x, mn), scale));
+  return static_cast<uint32_t>(fminf(fmaxf(q, 0.f), 3.f));
+}
+// The stored zero point of the uniform codec, so that (code - zero) * scale ~ code * scale + min.
+__device__ __forceinline__ float uniform_zero(float mn, float scale) { return __fdiv_rn(-mn, scale); }
+
 // Neighbouring FP32 values (towards -inf / +inf), zeros included.
 __device__ __forceinline__ float f32_prev(float d) {
   const int b = __float_as_int(d);

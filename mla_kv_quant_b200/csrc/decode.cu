@@ -125,9 +125,12 @@ __device__ void window_split(const DecodeArgs& a, uint8_t* smem, int b, int L) {
     const int h = u / nw, p = u % nw;
     const uint16_t* qh = qb + h * a.q_sh;
     const float* k = kw + p * (D + DR);
+    const int pos = p < n1 ? s1 + p : s2 + (p - n1);
+    const int64_t page = a.page_table[b * a.pt_stride + pos / kPage];
     float s = 0.f;
     for (int e = 0; e < D + DR; ++e) s = fmaf(bf16f(qh[e]), k[e], s);
-    pr[h * nw + p] = s * a.sm_scale;
+    // a row whose page is out of range takes no weight (the INT2 splits skip such tokens too)
+    pr[h * nw + p] = (page >= 0 && (page + 1) * kPage <= a.cache.num_slots) ? s * a.sm_scale : -INFINITY;
   }
   __syncthreads();
   if (tid < H) {
@@ -135,7 +138,8 @@ __device__ void window_split(const DecodeArgs& a, uint8_t* smem, int b, int L) {
     for (int p = 0; p < nw; ++p) m = fmaxf(m, pr[tid * nw + p]);
     float l = 0.f;
     for (int p = 0; p < nw; ++p) {
-      const float e = __expf(pr[tid * nw + p] - m);
+      const float x = pr[tid * nw + p];
+      const float e = x != -INFINITY ? __expf(x - m) : 0.f;
       pr[tid * nw + p] = e;
       l += e;
     }
@@ -149,11 +153,11 @@ __device__ void window_split(const DecodeArgs& a, uint8_t* smem, int b, int L) {
     float o = 0.f;
     for (int p = 0; p < nw; ++p) o = fmaf(pr[h * nw + p], kw[p * (D + DR) + j], o);
     const int64_t row = (static_cast<int64_t>(b) * H + h) * S + a.num_splits;
-    a.part_o[row * D + j] = nw > 0 ? o / wl[h] : 0.f;
+    a.part_o[row * D + j] = wl[h] > 0.f ? o / wl[h] : 0.f;
   }
   if (tid < H) {
     const int64_t row = (static_cast<int64_t>(b) * H + tid) * S + a.num_splits;
-    a.part_lse[row] = nw > 0 ? wm[tid] + logf(wl[tid]) : -INFINITY;
+    a.part_lse[row] = wl[tid] > 0.f ? wm[tid] + logf(wl[tid]) : -INFINITY;
   }
 }
 
@@ -264,7 +268,8 @@ __global__ void __launch_bounds__(kWinHeads * 32) window_rows_kernel(const Decod
   {  // warp = head, lane = row
     const int h = warp;
     float sc = -INFINITY;
-    if (lane < nw) {  // four interleaved partial sums (KW is a multiple of 4)
+    if (lane < nw && rslot[lane] >= 0) {  // four interleaved partial sums (KW is a multiple of 4);
+                                          // a row whose page is out of range takes no weight
       const float* k = kw + lane * KP;
       const float* qh = qf + h * KW;
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -278,7 +283,7 @@ __global__ void __launch_bounds__(kWinHeads * 32) window_rows_kernel(const Decod
     float m = sc;
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
-    const float ex = lane < nw ? __expf(sc - m) : 0.f;
+    const float ex = sc != -INFINITY ? __expf(sc - m) : 0.f;
     pr[h * kMaxWindow + lane] = ex;
     __syncwarp();
     if (lane == 0) {  // the sum in row order, as window_split
@@ -313,11 +318,11 @@ __global__ void __launch_bounds__(kWinHeads * 32) window_rows_kernel(const Decod
     const int64_t row = (static_cast<int64_t>(b) * H + h0 + h) * S + a.num_splits;
 #pragma unroll
     for (int c = 0; c < JT; ++c)
-      a.part_o[row * D + tid + c * kWinHeads * 32] = nw > 0 ? o[h][c] / wl[h] : 0.f;
+      a.part_o[row * D + tid + c * kWinHeads * 32] = wl[h] > 0.f ? o[h][c] / wl[h] : 0.f;
   }
   if (tid < kWinHeads) {
     const int64_t row = (static_cast<int64_t>(b) * H + h0 + tid) * S + a.num_splits;
-    a.part_lse[row] = nw > 0 ? wm[tid] + logf(wl[tid]) : -INFINITY;
+    a.part_lse[row] = wl[tid] > 0.f ? wm[tid] + logf(wl[tid]) : -INFINITY;
   }
 }
 
@@ -963,7 +968,8 @@ __global__ void __launch_bounds__(kMwThreads, 2) merge_window_kernel(const Decod
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
-    if (lane == 0) sc[hw][p] = acc * a.sm_scale;
+    // a row whose page is out of range takes no weight (the INT2 splits skip such tokens too)
+    if (lane == 0) sc[hw][p] = rslot[p] >= 0 ? acc * a.sm_scale : -INFINITY;
   }
   __syncthreads();
   if (warp < kMwHeads) {  // window softmax of head h0 + warp
@@ -971,13 +977,13 @@ __global__ void __launch_bounds__(kMwThreads, 2) merge_window_kernel(const Decod
     float m = x;
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
-    const float e = lane < nw ? __expf(x - m) : 0.f;
+    const float e = x != -INFINITY ? __expf(x - m) : 0.f;
     float l = e;
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
     if (lane < nw) sc[warp][lane] = e;
     if (lane == 0) {
-      stat[warp][0] = nw > 0 ? m + logf(l) : -INFINITY;
+      stat[warp][0] = l > 0.f ? m + logf(l) : -INFINITY;
       stat[warp][1] = l;
     }
   }
@@ -1004,7 +1010,7 @@ __global__ void __launch_bounds__(kMwThreads, 2) merge_window_kernel(const Decod
     for (int c = 0; c < 8; ++c) ow[c] = fmaf(e, v[c], ow[c]);
   }
   const float lse_w = stat[hh][0];
-  const float il = nw > 0 ? 1.f / stat[hh][1] : 0.f;
+  const float il = stat[hh][1] > 0.f ? 1.f / stat[hh][1] : 0.f;
 #pragma unroll
   for (int c = 0; c < 8; ++c) ow[c] *= il;
   const int64_t row = static_cast<int64_t>(b) * heads + h0 + hh;

@@ -134,12 +134,52 @@ __device__ __noinline__ void exact_code_words(uint32_t taddr, float mean, float 
   }
 }
 
+// Uniform min/max codes of one (row, group) (ROLAQ_CODEC_UNIFORM, OSCAR's baseline codec):
+// the group's FP32 minimum and maximum, then one IEEE quotient per element.  Warp-collective
+// (TMEM loads); its own instantiation of the kernel, so the learned-codec path is unchanged.
+__device__ __forceinline__ void uniform_code_words(uint32_t taddr, uint32_t* words, float* scale_out,
+                                                float* zero_out) {
+  uint32_t r[32];
+  float mn = INFINITY, mx = -INFINITY;
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    tmem_ld32(taddr + c * 32, r);
+    tmem_wait_ld();
+    reg_fence(r);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      mn = fminf(mn, __uint_as_float(r[j]));
+      mx = fmaxf(mx, __uint_as_float(r[j]));
+    }
+  }
+  const float scale = uniform_scale(mn, mx);
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    tmem_ld32(taddr + c * 32, r);
+    tmem_wait_ld();
+    reg_fence(r);
+    uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const uint32_t code = uniform_code(__uint_as_float(r[j]), mn, scale);
+      if (j < 16)
+        w0 |= code << (2 * j);
+      else
+        w1 |= code << (2 * (j - 16));
+    }
+    words[2 * c] = w0;
+    words[2 * c + 1] = w1;
+  }
+  *scale_out = scale;
+  *zero_out = uniform_zero(mn, scale);
+}
+
 // The epilogue of one (row, group) of an accumulator: the thread's TMEM lane holds the row's
 // 128 rotated values of the group at columns taddr .. taddr + 127.  kPlain: the rotated row
 // (FP32 and / or BF16).  Otherwise the codec (mean, population variance, Lloyd codes from
 // exact bounds), the packed codes and (scale, zero) by slot, the group's share of the k_pe
 // copy, once per row (group 0) the slot <-> ring maps; window rows also go to the BF16 ring.
-template <bool kPlain>
+template <bool kPlain, bool kUniform>
 __device__ __forceinline__ void epilogue_row_group(const WriterArgs& args, uint32_t taddr, int64_t row, bool valid,
                                                    int group, int d) {
   uint32_t r[32];
@@ -171,6 +211,11 @@ __device__ __forceinline__ void epilogue_row_group(const WriterArgs& args, uint3
       }
     }
   } else {
+    uint32_t words[8];
+    float scale, zero;
+    if constexpr (kUniform) {
+      uniform_code_words(taddr, words, &scale, &zero);
+    } else {
     // pass 1: mean
     GroupSum acc;
     acc.zero();
@@ -216,7 +261,6 @@ __device__ __forceinline__ void epilogue_row_group(const WriterArgs& args, uint3
     if (!exact_all)
       exact_all = !(sub_bound(b_lo, mean, &x_lo) && sub_bound(b_mid, mean, &x_mid) &&
                     sub_bound(b_hi, mean, &x_hi));
-    uint32_t words[8];
     if (__any_sync(0xFFFFFFFFu, exact_all)) {
       exact_code_words(taddr, mean, stdv, thr, words);  // rare: the whole warp, quotient per element
     } else {
@@ -239,8 +283,9 @@ __device__ __forceinline__ void epilogue_row_group(const WriterArgs& args, uint3
         words[2 * c + 1] = w1;
       }
     }
-    const float scale = __fmul_rn(args.codec.scale_factor, stdv);
-    const float zero = __fsub_rn(args.codec.zero_const, __fdiv_rn(mean, scale));
+    scale = __fmul_rn(args.codec.scale_factor, stdv);
+    zero = __fsub_rn(args.codec.zero_const, __fdiv_rn(mean, scale));
+    }
     RowMeta m{0, -1, false};
     if (valid) m = row_meta(args, row, args.slots[row]);
     if (valid && !m.ok && group == 0) report(args.err, ROLAQ_DEV_BAD_SLOT);
@@ -317,7 +362,7 @@ __device__ __forceinline__ void epilogue_prefetch(const WriterArgs& args, int64_
   }
 }
 
-template <bool kPlain>
+template <bool kPlain, bool kUniform = false>
 __global__ void __launch_bounds__(kWriterThreads, 1)
     writer_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                   const WriterArgs args) {
@@ -466,7 +511,7 @@ __global__ void __launch_bounds__(kWriterThreads, 1)
       const bool valid = row < args.n;
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(buf * kTileN);
-      epilogue_row_group<kPlain>(args, taddr, row, valid, group, d);
+      epilogue_row_group<kPlain, kUniform>(args, taddr, row, valid, group, d);
       tc_fence_before();
       mbar_arrive(&tempty[buf]);
     }
@@ -597,6 +642,20 @@ __global__ void __launch_bounds__(kSmThreads) small_writer_kernel(const uint16_t
       const float t3 = __fadd_rn(t2, __shfl_xor_sync(0xFFFFFFFFu, t2, 4));
       return __shfl_sync(0xFFFFFFFFu, t3, 0);
     };
+    uint32_t byte = 0;
+    float scale, zero;
+    if (args.codec.family == ROLAQ_CODEC_UNIFORM) {  // min / max over the warp's 128 values
+      float mn = fminf(fminf(v[0], v[1]), fminf(v[2], v[3])), mx = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) {
+        mn = fminf(mn, __shfl_xor_sync(0xFFFFFFFFu, mn, o));
+        mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+      }
+      scale = uniform_scale(mn, mx);
+      zero = uniform_zero(mn, scale);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) byte |= uniform_code(v[q], mn, scale) << (2 * q);
+    } else {
     const float mean = __fmul_rn(group_total([](float x) { return x; }), 1.0f / 128.0f);
     const float var = __fmul_rn(group_total([&](float x) {
                                   const float df = __fsub_rn(x, mean);
@@ -604,7 +663,6 @@ __global__ void __launch_bounds__(kSmThreads) small_writer_kernel(const uint16_t
                                 }), 1.0f / 128.0f);
     const float stdv = __fsqrt_rn(__fadd_rn(var, 1e-8f));
     const float thr = args.codec.threshold;
-    uint32_t byte = 0;
     if (stdv < 16777216.f) {  // exact bounds: three compares per element
       const float b_lo = quotient_bound(-thr, stdv), b_mid = quotient_bound_zero(stdv),
                   b_hi = quotient_bound(thr, stdv);
@@ -618,8 +676,9 @@ __global__ void __launch_bounds__(kSmThreads) small_writer_kernel(const uint16_t
 #pragma unroll
       for (int q = 0; q < 4; ++q) byte |= lloyd_code(__fsub_rn(v[q], mean), stdv, thr) << (2 * q);
     }
-    const float scale = __fmul_rn(args.codec.scale_factor, stdv);
-    const float zero = __fsub_rn(args.codec.zero_const, __fdiv_rn(mean, scale));
+    scale = __fmul_rn(args.codec.scale_factor, stdv);
+    zero = __fsub_rn(args.codec.zero_const, __fdiv_rn(mean, scale));
+    }
     const RowMeta m = row_meta_of(args, __shfl_sync(0xFFFFFFFFu, m_slot, 0), __shfl_sync(0xFFFFFFFFu, m_seq, 0),
                                   __shfl_sync(0xFFFFFFFFu, m_req, 0), __shfl_sync(0xFFFFFFFFu, m_pos, 0));
     if (!m.ok) {
@@ -694,9 +753,15 @@ int launch_writer(const uint16_t* x, int64_t ldx, const uint16_t* w, const Write
   static const bool attr_codec =
       cudaFuncSetAttribute(writer_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kWriterSmem) ==
       cudaSuccess;
-  if (!(plain ? attr_plain : attr_codec)) return ROLAQ_ECUDA;
+  static const bool attr_uniform =
+      cudaFuncSetAttribute(writer_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)kWriterSmem) == cudaSuccess;
+  const bool uniform = !plain && args.codec.family == ROLAQ_CODEC_UNIFORM;
+  if (!(plain ? attr_plain : (uniform ? attr_uniform : attr_codec))) return ROLAQ_ECUDA;
   if (plain) {
     writer_kernel<true><<<grid, kWriterThreads, kWriterSmem, stream>>>(mx, mw, args);
+  } else if (uniform) {
+    writer_kernel<false, true><<<grid, kWriterThreads, kWriterSmem, stream>>>(mx, mw, args);
   } else {
     writer_kernel<false><<<grid, kWriterThreads, kWriterSmem, stream>>>(mx, mw, args);
   }

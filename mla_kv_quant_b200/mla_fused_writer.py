@@ -3,8 +3,13 @@
 ``try_fast_decode_store`` keeps the reference's contract: it returns whether it
 handled the write, so the caller's fallback path stays in charge otherwise.  The
 reference ran ``c = c_kv.float() @ R`` as an FP32 cuBLAS GEMM and then one Triton
-launch; here one sm_100a launch (``rolaq_fused_write``) does the rotation on tcgen05,
-the codec, the packed scatter, the BF16 ``k_pe`` store and the s4r16 ring stores.
+launch (the Lloyd codec) or ``scatter_pack_rows`` + ``_aux`` (any other codec); here
+one sm_100a launch (``rolaq_fused_write``) does the rotation on tcgen05, the codec
+(learned / default Lloyd, or OSCAR's uniform min/max when the pool runs without
+Lloyd-Max), the packed scatter, the BF16 ``k_pe`` store and the s4r16 ring stores.
+A layer without a rotation is written unrotated (``c = c_kv``, the reference's
+``mla_fused_writer.py:146-149``): the identity matrix as the tcgen05 operand gives
+``c`` exactly.
 """
 
 from __future__ import annotations
@@ -12,7 +17,6 @@ from __future__ import annotations
 import torch
 
 from . import ops
-from .mla_latent_int2 import _LM_RATIO, _LM_THRESHOLDS
 
 _SUPPORTED = {(512, 64), (256, 32)}
 
@@ -34,22 +38,17 @@ def try_fast_decode_store(pool, layer_id, loc, c_kv, k_pe):
         or meta["req_pool_indices"].numel() != n
         or pool._selfcheck_budget > 0
         or pool._audit_budget > 0
-        or not (pool._lloyd_max and pool._bits == 2)
-        or pool.latent_rotation(layer_id, local=True) is None
+        or pool._bits != 2  # only 2-bit packed storage is built; the caller's path takes the rest
     ):
         return False
-    li = layer_id - pool.start_layer
     loc64 = loc.reshape(-1).to(torch.int64)
     pool._write_loc = loc64
-    params = pool._rolaq_quantizers[li]
-    threshold, gain = (params[0], params[1]) if params is not None else (_LM_THRESHOLDS[2], _LM_RATIO)
-    codec = ops.codec_serving(threshold, gain)
     ops.fused_write(
         c_kv.reshape(-1, pool.kv_lora_rank),
         k_pe.reshape(-1, pool.qk_rope_head_dim),
         loc64,
         pool.write_rotation_t(layer_id),
-        codec,
+        pool.codec(layer_id),
         pool.layer_view(layer_id),
         seq_lens=meta["seq_lens"],
         req_idx=meta["req_pool_indices"],

@@ -3,8 +3,9 @@
 
 ``scatter_pack_rows`` keeps the patched signature and check of
 ``deployment/patches/rolaq_sglang.patch:9-34``; the codec runs in
-``rolaq_scatter_pack_rows``.  Only the Lloyd INT2 codec is implemented; the OSCAR
-uniform min/max baseline (``lloyd_max=False``) is rejected.
+``rolaq_scatter_pack_rows``: the learned / default Lloyd INT2 codec, or with
+``lloyd_max=False`` OSCAR's uniform min/max INT2 baseline (``mla_quant/oscar.py:91-101``).
+Only 2-bit storage is built; other widths raise ``NotImplementedError``.
 """
 
 from __future__ import annotations
@@ -24,13 +25,17 @@ def scatter_pack_rows(x, slots, codes_buf, params_buf, group_size, lloyd_max, bi
     """Quantize ``x`` (``[n, D]``, rotated frame) into ``codes/params`` at ``slots``."""
     if quantizer_params is not None and (not lloyd_max or bits != 2):
         raise ValueError("Learned threshold/gain require the INT2 Lloyd writer")
-    if not lloyd_max or bits != 2:
-        raise NotImplementedError("only the Lloyd-Max INT2 codec is implemented")
+    if bits != 2:
+        raise NotImplementedError("only 2-bit packed storage is implemented")
     if group_size != 128:
         raise ValueError("group_size must be 128")
     n = x.shape[0]
     if n == 0:
         return
     x = x.contiguous().to(torch.float32)
-    threshold, gain = quantizer_params if quantizer_params is not None else (_LM_THRESHOLDS[2], _LM_RATIO)
-    ops.scatter_pack_rows(x, slots.contiguous(), codes_buf, params_buf, ops.codec_serving(threshold, gain))
+    if lloyd_max:
+        threshold, gain = quantizer_params if quantizer_params is not None else (_LM_THRESHOLDS[2], _LM_RATIO)
+        codec = ops.codec_serving(threshold, gain)
+    else:
+        codec = ops.codec_uniform()
+    ops.scatter_pack_rows(x, slots.contiguous(), codes_buf, params_buf, codec)

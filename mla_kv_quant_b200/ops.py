@@ -49,6 +49,12 @@ def codec_serving(threshold: float, gain: float) -> _lib.Codec:
     return _lib.Codec(_f32(threshold), _f32(SPAN / 3.0 * float(gain)), _f32(-LLOYD_MAX_CENTROIDS[0] / (SPAN / 3.0)))
 
 
+def codec_uniform() -> _lib.Codec:
+    """OSCAR's uniform min/max INT2 codec (``mla_quant/oscar.py:91-101``), the writer's
+    baseline when the pool runs without Lloyd-Max (``mla_fused_writer.py:194-224``)."""
+    return _lib.Codec(0.0, 0.0, 0.0, _lib.CODEC_UNIFORM)
+
+
 def _check(t: torch.Tensor, name: str, dtype=None, ndim=None):
     if not isinstance(t, torch.Tensor):
         raise TypeError(f"{name} must be a tensor")
@@ -282,9 +288,13 @@ def merge_partials(part_o: torch.Tensor, part_lse: torch.Tensor, out_bf16: torch
               _lib.ptr(out_lse), _lib.stream_ptr())
 
 
-def default_num_splits(batch: int, max_ctx: int, sm_count: int = 148, ctas_per_sm: int = 2) -> int:
+def default_num_splits(batch: int, max_ctx: int, sm_count: int = 148, ctas_per_sm: int | None = None,
+                       latent_dim: int = 512, rope_dim: int = 64, heads: int = 16) -> int:
     """Pick the number of INT2 KV splits per request so that ``batch * splits`` CTAs
-    fill whole waves of the GPU and each split keeps at least 4 pages."""
+    fill whole waves of the GPU and each split keeps at least 4 pages.  The tcgen05
+    kernel of the 512/64/16 shape holds one CTA per SM; the warp-MMA kernel two."""
+    if ctas_per_sm is None:
+        ctas_per_sm = 1 if (latent_dim, rope_dim, heads) == (512, 64, 16) else 2
     pages = max(1, math.ceil(max_ctx / PAGE))
     slots = sm_count * ctas_per_sm
     best, best_cost = 1, float("inf")

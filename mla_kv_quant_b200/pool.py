@@ -82,6 +82,7 @@ class PackedLatentPool:
         self.rotations = dict(rotations or {})
         self._rolaq_quantizers = list(quantizer_params) if quantizer_params is not None else [None] * layer_num
         self._rot_t: dict[int, tuple[int, torch.Tensor]] = {}
+        self._identity_t: torch.Tensor | None = None
 
     # ---- construction from the reference's environment flags ---------------------------
     @classmethod
@@ -117,10 +118,15 @@ class PackedLatentPool:
         return self.rotations.get(layer_id)
 
     def write_rotation_t(self, layer_id: int) -> torch.Tensor:
-        """``bf16(R)^T`` on the pool device, cached per layer (the tcgen05 B operand)."""
+        """``bf16(R)^T`` on the pool device, cached per layer (the tcgen05 B operand).  A
+        layer without a rotation gets the identity: the writer then stores ``c = c_kv``
+        exactly (BF16 values times 1 accumulate exactly in FP32), as the reference's
+        writer does without a rotation (``mla_fused_writer.py:146-149``)."""
         r = self.latent_rotation(layer_id)
         if r is None:
-            raise ValueError(f"no rotation for layer {layer_id}")
+            if self._identity_t is None:
+                self._identity_t = torch.eye(self.kv_lora_rank, dtype=torch.bfloat16, device=self.device)
+            return self._identity_t
         cached = self._rot_t.get(layer_id)
         if cached is None or cached[0] != id(r):
             rt = r.to(device=self.device, dtype=torch.bfloat16).t().contiguous()
@@ -134,7 +140,10 @@ class PackedLatentPool:
                              self.hp_row_of_slot, self.hp_owner_of_row, self._win_p, self._win_r, self._max_reqs)
 
     def codec(self, layer_id: int):
-        """Serving-path codec scalars of a layer (learned, or the Lloyd-Max defaults)."""
+        """Serving-path codec of a layer: the learned Lloyd scalars, the Lloyd-Max defaults,
+        or OSCAR's uniform min/max codec when the pool runs without Lloyd-Max."""
+        if not self._lloyd_max:
+            return ops.codec_uniform()
         li = layer_id - self.start_layer
         params = self._rolaq_quantizers[li]
         if params is None:

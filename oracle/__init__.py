@@ -17,6 +17,10 @@ What is restated here, and from where (paths are inside noforit/mla_kv_quant):
   window rows, the math implied by ``deployment/patches/rolaq_sglang.patch:51-111,
   205-248`` and ``deployment/sglang/srt/mem_cache/rolaq_mla.py:56-71``.
 * ``window``  -- the sink/recent token states of ``mla_quant/cache.py:775-800``.
+* ``quantizer`` -- ``rotate_quantize`` (``mla_quant/quantizer.py:102-124``), the HF
+  quantize-dequantize path, on the CPU; also the timed fallback of the CPU QDQ baseline.
+* ``codec.encode_uniform`` -- OSCAR's uniform min/max INT2 baseline codec
+  (``mla_quant/oscar.py:91-101``).
 
 Parity status: the codec arithmetic is pinned against golden vectors produced by
 importing the reference itself (``tests/golden/make_golden.py``).  The packed byte
@@ -26,4 +30,4 @@ restates the semantics of the reference's call sites, and byte-level parity
 against upstream is unpinned.
 """
 
-from . import codec, writer, decode, window  # noqa: F401
+from . import codec, writer, decode, window, quantizer  # noqa: F401

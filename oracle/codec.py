@@ -121,6 +121,43 @@ def qdq(x: np.ndarray, t32, scale_factor32, zero_const32=np.float32(ZERO_CONST))
     return dequant(codes, scale, zero)
 
 
+# ---- OSCAR's uniform min/max INT2 baseline ------------------------------------------
+
+
+def encode_uniform(x: np.ndarray):
+    """Rotated FP32 rows ``[n, D]`` -> (codes ``[n, D]``, scale ``[n, NG]``, minimum ``[n, NG]``).
+
+    Restates ``uniform_int2_qdq`` (``mla_quant/oscar.py:91-101``): per 128-group
+    ``scale = (max - min) / 3`` where ``|max - min| > 1e-8`` (the scalar rounded to FP32),
+    else 1; ``code = clamp(round((x - min) / scale), 0, 3)`` with round-half-to-even
+    (``torch.round``, ``np.rint``); every operation in FP32.
+    """
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n, d = x.shape
+    g = x.reshape(n, d // GROUP, GROUP)
+    mn = g.min(axis=-1)
+    mx = g.max(axis=-1)
+    rng = mx - mn
+    scale = np.where(np.abs(rng) > np.float32(1e-08), rng / np.float32(3.0), np.float32(1.0)).astype(np.float32)
+    q = (g - mn[..., None]) / scale[..., None]
+    codes = np.clip(np.rint(q), 0, 3).astype(np.uint8)
+    return codes.reshape(n, d), scale, mn.astype(np.float32)
+
+
+def uniform_qdq(x: np.ndarray) -> np.ndarray:
+    """``codes * scale + min`` in FP32 (the reference's reconstruction)."""
+    codes, scale, mn = encode_uniform(x)
+    n, d = codes.shape
+    c = codes.reshape(n, d // GROUP, GROUP).astype(np.float32)
+    return (c * scale[..., None] + mn[..., None]).reshape(n, d).astype(np.float32)
+
+
+def uniform_params(scale: np.ndarray, mn: np.ndarray) -> np.ndarray:
+    """The cache's (scale, zero) of the uniform codec: zero = FP32(-min / scale), so that
+    the reader's ``(code - zero) * scale`` reconstructs ``code * scale + min``."""
+    return params_array(scale, (-mn / scale).astype(np.float32))
+
+
 # ---- packed byte layout (this build's cache format) -------------------------------
 # Code of latent element j lives in byte j // 4 of the slot's row, bits 2*(j % 4).
 

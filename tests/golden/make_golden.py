@@ -11,6 +11,8 @@ it writes; the tests never import the reference.
 
 Fixtures written:
 
+* ``uniform.npz``   -- ``uniform_int2_qdq`` (``mla_quant/oscar.py:91-101``), OSCAR's
+  uniform min/max INT2 baseline, on seeded rows plus exact-tie and constant groups.
 * ``codec.npz``     -- ``oscar_lloyd_int2_qdq`` (``mla_quant/oscar.py:120-144``) on
   seeded FP32 rows for several (threshold, gain) pairs, plus the HF-path scalar
   handling through ``quantize_learned`` (``mla_quant/quantizer.py:31-35, 73-82``).
@@ -77,6 +79,7 @@ def signal_gain(t: float) -> float:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="checkout of noforit/mla_kv_quant")
+    ap.add_argument("--only", choices=["uniform"], default=None, help="write only this fixture")
     args = ap.parse_args()
     ref = Path(args.reference).resolve()
     sys.path.insert(0, str(ref))
@@ -96,6 +99,20 @@ def main() -> None:
 
     configure_reference_numerics()
     torch.manual_seed(0)
+
+    # ---- uniform min/max baseline codec (mla_quant/oscar.py:91-101) ----------------------
+    from mla_quant.oscar import uniform_int2_qdq
+
+    xu = latents(24, 512, seed=3)
+    ties = np.tile(np.float32([0.0, 0.5, 1.5, 2.5, 3.0, 1.0, 2.0, 0.25]), (1, 64))  # scale 1: exact .5 ties
+    neg = ties - np.float32(7.0)
+    xu = np.concatenate(
+        [xu, ties, neg, np.full((1, 512), -2.5, np.float32), (np.arange(512, dtype=np.float32)[None, :] * 0.003)], 0
+    ).astype(np.float32)
+    np.savez_compressed(HERE / "uniform.npz", x=xu, deq=uniform_int2_qdq(torch.from_numpy(xu), 128).numpy())
+    if args.only == "uniform":
+        print("wrote uniform.npz to", HERE)
+        return
 
     # ---- codec --------------------------------------------------------------------
     x = latents(40, 512, seed=0)

@@ -1,0 +1,122 @@
+"""Parity at the shapes the benchmark times.
+
+* Writer, config 1: 8 requests x 16384 tokens = 131072 rows in one launch.  The
+  persistent tcgen05 grid (one CTA per SM, four groups) then runs ~28 row tiles per
+  CTA, so every TMEM accumulator, every epilogue warp set and many mbarrier phase
+  flips are exercised.  Codes/params are bit-exact against the oracle codec on the
+  kernel's own FP32 rotation; against the reference FP32 GEMM rotation at most 1e-4
+  of the codes differ (rounding ties); k_pe, ring rows and maps equal the oracle
+  writer's.
+* Decode, config 2: 64 requests x 16384 tokens with the benchmark's default split
+  count (9), through the caller-scratch and the static-scratch entry points, a seeded
+  subset of 8 requests against the FP64 oracle (max-abs <= 2e-2, cosine >= 0.9995).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_helpers import GpuPool, bits, cosine, fill_requests, oracle_scalars, rotate_cpu
+from mla_kv_quant_b200 import ops, synth
+from oracle import codec as ocodec
+from oracle import decode as odecode
+from oracle import writer as owriter
+
+pytestmark = pytest.mark.gpu
+
+CTX = 16384
+
+
+def test_writer_config1_every_tile_slot_and_phase():
+    d, dr, reqs = 512, 64, 8
+    n = reqs * CTX
+    pt, num_slots = synth.page_table(reqs, CTX, seed=41, device="cuda")
+    pool = GpuPool(num_slots, d, dr, max_reqs=reqs)
+    x = synth.latents(n, d, seed=42, device="cuda")
+    pe = synth.normal_bf16((n, dr), seed=43, device="cuda")
+    r = synth.rotation(d, seed=44)
+    rt = r.to(torch.bfloat16).t().contiguous().cuda()
+    pos = torch.arange(CTX, device="cuda").repeat(reqs)
+    req = torch.arange(reqs, device="cuda").repeat_interleave(CTX)
+    slots = (pt[req, pos // 64].long() * 64 + pos % 64).contiguous()
+    seq = torch.full((n,), CTX, dtype=torch.int32, device="cuda")
+    codec = ops.codec_serving(0.78, synth.signal_gain(0.78))
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ops.fused_write(x, pe, slots, rt, codec, pool.view(), seq_lens=seq, req_idx=req, positions=pos.to(torch.int32),
+                    err=err)
+    rot = torch.empty(n, d, device="cuda")
+    ops.rotate_rows(x, rt, out_f32=rot)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    s = slots.cpu().numpy()
+    rot_np = rot.cpu().numpy()
+    oc, osc, oze = ocodec.encode(rot_np, *oracle_scalars(codec))
+    assert np.array_equal(pool.codes.cpu().numpy()[s], ocodec.pack(oc))
+    assert np.array_equal(pool.params.cpu().numpy()[s], ocodec.params_array(osc, oze))
+    # k_pe, ring rows, maps: the oracle writer applied to the same rotated rows
+    opool = owriter.Pool(num_slots, d, dr, reqs, 4, 16)
+    t32, sf32, z32 = oracle_scalars(codec)
+    owriter.write(opool, rot_np, bits(pe), s, seq.cpu().numpy(), req.cpu().numpy(), t32, sf32,
+                  positions=pos.cpu().numpy(), zero_const32=z32)
+    assert np.array_equal(bits(pool.rope), opool.rope)
+    assert np.array_equal(bits(pool.hp), opool.hp)
+    assert np.array_equal(pool.rows.cpu().numpy(), opool.rows)
+    assert np.array_equal(pool.owners.cpu().numpy(), opool.owners)
+    # against the reference FP32 GEMM rotation: codes differ only at rounding ties
+    rc, _, _ = ocodec.encode(rotate_cpu(x, r), *oracle_scalars(codec))
+    got = ocodec.unpack(pool.codes.cpu().numpy()[s], d)
+    assert np.mean(got != rc) <= 1e-4
+
+
+@pytest.fixture(scope="module")
+def config2_pool():
+    d, dr, b = 512, 64, 64
+    seq_lens = [CTX] * b
+    g = torch.Generator().manual_seed(51)
+    pages = CTX // 64
+    pt = (torch.randperm(b * pages, generator=g) + 1).to(torch.int32).reshape(b, pages).cuda()
+    pool = GpuPool(64 * (b * pages + 1), d, dr, max_reqs=b, sink=4, recent=16)
+    fill_requests(pool, seq_lens, pt, synth.rotation(d, seed=52), ops.codec_serving(0.85, synth.signal_gain(0.85)),
+                  seed=53)
+    return pool, pt, seq_lens
+
+
+@pytest.mark.parametrize("entry", ["caller_scratch", "static_scratch"])
+def test_decode_config2_default_splits(config2_pool, entry):
+    import ctypes
+
+    from mla_kv_quant_b200 import _lib
+
+    pool, pt, seq_lens = config2_pool
+    d, dr, h = 512, 64, 16
+    b = len(seq_lens)
+    splits = ops.default_num_splits(b, CTX)
+    assert splits == 9
+    q = synth.normal_bf16((b, h, d + dr), seed=54, device="cuda")
+    sl = torch.tensor(seq_lens, dtype=torch.int32, device="cuda")
+    out = torch.full((b, h, d), float("nan"), dtype=torch.bfloat16, device="cuda")
+    lse = torch.full((b, h), float("nan"), device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    sm = 1.0 / np.sqrt(192.0)
+    if entry == "caller_scratch":
+        part_o = torch.empty(b, h, splits + 1, d, device="cuda")
+        part_lse = torch.empty(b, h, splits + 1, device="cuda")
+        ops.packed_decode(q, pool.view(), pt, sl, sm, splits, part_o, part_lse, out, out_lse=lse, err=err)
+    else:
+        lib = _lib.load()
+        cs = pool.view().c_struct()
+        stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        rc = lib.rolaq_packed_decode_static(q.data_ptr(), q.stride(0), q.stride(1), b, h, ctypes.byref(cs),
+                                            pt.data_ptr(), pt.stride(0), pt.shape[1], sl.data_ptr(), None, sm, splits,
+                                            out.data_ptr(), out.stride(0), out.stride(1), lse.data_ptr(),
+                                            err.data_ptr(), stream)
+        assert rc == 0, lib.rolaq_last_error()
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    sub = sorted(np.random.default_rng(55).choice(b, size=8, replace=False).tolist())
+    ref, ref_lse = odecode.decode(pool.to_oracle(), bits(q), pt.cpu().numpy(), seq_lens, sm, requests=sub)
+    o = out.float().cpu().numpy()
+    for i in sub:
+        assert np.abs(o[i] - ref[i]).max() <= 2e-2, f"request {i}"
+        assert cosine(o[i], ref[i]) >= 0.9995
+    assert np.allclose(lse.cpu().numpy()[sub], ref_lse[sub], atol=2e-3)

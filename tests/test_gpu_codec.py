@@ -88,3 +88,49 @@ def test_prepare_gf_splits():
     ops.prepare_gf_splits(s, q, m)
     assert q.tolist() == [1, 1, 1, 4, 128]
     assert m.tolist() == [2, 2, 2, 5, 129]
+
+
+def _uniform_rows(n, d, seed):
+    x = _rows(n, d, seed)
+    x[4] = torch.tensor([0.0, 0.5, 1.5, 2.5, 3.0, 1.0, 2.0, 0.25]).repeat(d // 8)  # scale 1: exact .5 ties
+    x[5] = x[4] - 7.0
+    return x
+
+
+@pytest.mark.parametrize("d", [512, 256])
+def test_scatter_pack_uniform_bit_exact(d):
+    """OSCAR's uniform min/max codec (lloyd_max=False) through the scatter-pack kernel."""
+    from mla_kv_quant_b200.mla_latent_int2 import scatter_pack_rows
+
+    n, num_slots = 300, 1024
+    x = _uniform_rows(n, d, seed=d + 1)
+    slots = torch.randperm(num_slots, generator=torch.Generator().manual_seed(6))[:n]
+    codes = torch.zeros(num_slots, d // 4, dtype=torch.uint8, device="cuda")
+    params = torch.zeros(num_slots, d // 128, 2, dtype=torch.float32, device="cuda")
+    scatter_pack_rows(x.cuda(), slots.cuda().to(torch.int32), codes, params, 128, lloyd_max=False)
+    torch.cuda.synchronize()
+    oc, osc, omn = ocodec.encode_uniform(x.numpy())
+    s = slots.numpy()
+    assert np.array_equal(codes.cpu().numpy()[s], ocodec.pack(oc))
+    assert np.array_equal(params.cpu().numpy()[s], ocodec.uniform_params(osc, omn))
+
+
+@pytest.mark.parametrize("d", [512, 256])
+@pytest.mark.parametrize("n", [64, 1000])
+def test_fused_write_uniform_bit_exact(d, n):
+    """The fused writer with the uniform codec (n = 64: the SIMT small-batch kernel; 1000:
+    the tcgen05 kernel) against the oracle codec on the kernel's own FP32 rotation."""
+    from mla_kv_quant_b200 import synth
+
+    x = synth.latents(n, d, seed=n + d, device="cuda")
+    rt = synth.rotation(d, seed=7).to(torch.bfloat16).t().contiguous().cuda()
+    codes = torch.zeros(n + 64, d // 4, dtype=torch.uint8, device="cuda")
+    params = torch.zeros(n + 64, d // 128, 2, dtype=torch.float32, device="cuda")
+    slots = torch.arange(64, 64 + n, device="cuda")
+    ops.encode_rows(x, rt, ops.codec_uniform(), codes, params, slots=slots)
+    rot = torch.empty(n, d, device="cuda")
+    ops.rotate_rows(x, rt, out_f32=rot)
+    torch.cuda.synchronize()
+    oc, osc, omn = ocodec.encode_uniform(rot.cpu().numpy())
+    assert np.array_equal(codes.cpu().numpy()[64:], ocodec.pack(oc))
+    assert np.array_equal(params.cpu().numpy()[64:], ocodec.uniform_params(osc, omn))

@@ -13,6 +13,7 @@ import torch
 from gpu_helpers import GpuPool, bits, cosine, fill_requests
 from mla_kv_quant_b200 import _lib, ops, synth
 from oracle import decode as odecode
+from oracle import writer as owriter
 
 pytestmark = pytest.mark.gpu
 
@@ -201,6 +202,41 @@ def test_decode_bad_page_is_reported():
     torch.cuda.synchronize()
     assert int(err.item()) & _lib.DEV_BAD_PAGE
     assert torch.isfinite(out.float()).all()
+
+
+@pytest.mark.parametrize("d,dr,h", [(512, 64, 16), (256, 32, 40)])
+@pytest.mark.parametrize("bad_page", [0, 4])
+def test_decode_bad_window_page_is_masked(d, dr, h, bad_page):
+    """A window page outside the pool is reported, and its rows take no weight: the output
+    equals the oracle's attention over the remaining tokens (page 0 holds the sink rows,
+    page 4 the recent rows of a 300-token request)."""
+    L = 300
+    pool, pt = _setup(d, dr, [L], seed=13)
+    opool = pool.to_oracle()
+    pt_ok = pt.cpu().numpy()
+    pt = pt.clone()
+    pt[0, bad_page] = 10_000  # outside the pool
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = torch.empty(1, h, d, dtype=torch.bfloat16, device="cuda")
+    lse = torch.empty(1, h, device="cuda")
+    q = synth.normal_bf16((1, h, d + dr), seed=1, device="cuda")
+    sm = 1.0 / np.sqrt(192.0)
+    ops.packed_decode(q, pool.view(), pt, torch.tensor([L], dtype=torch.int32, device="cuda"), sm, 2,
+                      torch.empty(1, h, 3, d, device="cuda"), torch.empty(1, h, 3, device="cuda"), out, out_lse=lse,
+                      err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) & _lib.DEV_BAD_PAGE
+    # the oracle over the tokens whose page is valid
+    slots = odecode.token_slots(pt_ok[0], L)
+    lat = odecode.latent_rows(opool, slots, L)
+    pe = owriter.bf16_to_f32(opool.rope[slots]).astype(np.float64)
+    keep = np.arange(L) // 64 != bad_page
+    qf = owriter.bf16_to_f32(bits(q)).astype(np.float64)[0]
+    ref, ref_lse = odecode.attend(qf, lat[keep], pe[keep], sm)
+    o = out[0].float().cpu().numpy()
+    assert np.max(np.abs(o - ref) - half_ulp_bf16(ref)) <= 2e-2
+    assert cosine(o, ref) >= 0.9995
+    assert np.allclose(lse[0].cpu().numpy(), ref_lse, atol=2e-3)
 
 
 def test_merge_partials_matches_oracle():

@@ -14,6 +14,7 @@ from mla_kv_quant_b200.mla_packed_decode import packed_mla_decode_gf_fwd, prepar
 from mla_kv_quant_b200.pool import PackedLatentPool
 from mla_kv_quant_b200.quantizer import LearnedRotationQuantizer, rotate_quantize
 from mla_kv_quant_b200.rolaq_mla import fold_read_rotation
+from oracle import codec as ocodec
 from oracle import decode as odecode
 from oracle import writer as owriter
 
@@ -173,3 +174,39 @@ def test_fold_read_rotation_matches_reference_golden(golden_dir):
     # accumulation order only: identical except one-ulp BF16 rounding flips
     assert (diff == 0).float().mean() >= 0.97
     assert torch.all(diff <= ref.abs() * 2 ** -7 + 1e-6)
+
+
+@pytest.mark.parametrize("lloyd_max", [True, False])
+def test_decode_write_unrotated_and_uniform(monkeypatch, lloyd_max):
+    """The writer plugin handles what the reference's handles (mla_fused_writer.py:
+    142-149, 194-224): a layer without a rotation is stored as c = c_kv, and a pool
+    without Lloyd-Max stores OSCAR's uniform min/max codes; both return True."""
+    monkeypatch.setenv("SGLANG_ROLAQ_MLA_FUSED_DECODE_WRITE", "1")
+    d, dr, b = 512, 64, 5
+    rot = {0: synth.rotation(d, 7)}  # layer 1 has no rotation
+    pool = PackedLatentPool(64 * 8, 2, max_reqs=b, rotations=rot, lloyd_max=lloyd_max)
+    slots = torch.tensor([70, 130, 200, 260, 333], device="cuda")
+    seq = torch.tensor([9, 30, 64, 65, 200], dtype=torch.int32, device="cuda")
+    req = torch.arange(b, device="cuda")
+    pool.set_window_meta(True, seq, req)
+    for li in range(2):
+        x = synth.latents(b, d, seed=li + 3, device="cuda")
+        pe = synth.normal_bf16((b, dr), seed=li + 4, device="cuda")
+        assert try_fast_decode_store(pool, li, slots, x, pe)
+        torch.cuda.synchronize()
+        if li == 1:
+            c = x.float().cpu().numpy()  # unrotated: exactly the BF16 input
+        else:
+            rot_gpu = torch.empty(b, d, device="cuda")
+            ops.rotate_rows(x, pool.write_rotation_t(li), out_f32=rot_gpu)
+            c = rot_gpu.cpu().numpy()
+        s = slots.cpu().numpy()
+        if lloyd_max:
+            oc, osc, oze = ocodec.encode(c, *oracle_scalars(pool.codec(li)))
+            prm = ocodec.params_array(osc, oze)
+        else:
+            oc, osc, omn = ocodec.encode_uniform(c)
+            prm = ocodec.uniform_params(osc, omn)
+        assert np.array_equal(pool.c_codes[li].cpu().numpy()[s], ocodec.pack(oc))
+        assert np.array_equal(pool.c_params[li].cpu().numpy()[s], prm)
+        assert np.array_equal(bits(pool.rope_buf[li])[s], bits(pe))

@@ -7,7 +7,7 @@ quantize_learned and rotate_quantize (noforit/mla_kv_quant) on seeded inputs.
 import numpy as np
 import pytest
 
-from oracle import codec, decode, window, writer
+from oracle import codec, decode, quantizer, window, writer
 
 
 def _flips(ours, ref, scale):
@@ -71,17 +71,13 @@ def test_rotate_quantize_restatement(golden_dir, d):
     r = z[f"r{d}"]
     lat = writer.bf16_to_f32(z[f"lat{d}"].reshape(-1, d))
     t, g = z[f"tg{d}"]
-    rot = codec.rotate_reference(lat, r)
-    deq = codec.qdq(rot, *codec.hf_scalars(t, g))
-    deq_bf = writer.bf16_round(deq)
-    reff = torch.from_numpy(r).to(torch.bfloat16).float()
-    restored = writer.bf16_round((torch.from_numpy(deq_bf) @ reff.T).numpy())
+    restored = quantizer.rotate_quantize(lat, r, t, g)
     ref = writer.bf16_to_f32(z[f"out_plain{d}"].reshape(-1, d))
     # identical except where a ULP of mean/std moved a BF16 rounding
     assert np.mean(restored == ref) > 0.99
     assert np.max(np.abs(restored - ref)) < 0.05 * np.max(np.abs(ref))
     mask = z[f"mask{d}"]
-    masked = np.where(mask[:, None], lat, restored)
+    masked = quantizer.rotate_quantize(lat, r, t, g, mask=mask)
     refm = writer.bf16_to_f32(z[f"out_masked{d}"].reshape(-1, d))
     assert np.array_equal(masked[mask], refm[mask])
 
@@ -125,3 +121,15 @@ def test_oracle_writer_and_decode_small():
     o2, l2 = decode.attend(qf, lat[37:], pe[37:], 0.1)
     om, lm = decode.merge(np.stack([o1, o2]), np.stack([l1, l2]))
     assert np.allclose(om, out[0]) and np.allclose(lm, lse[0])
+
+
+def test_uniform_codec_restatement(golden_dir):
+    """OSCAR's uniform min/max INT2 codec: the restated codes reconstruct the reference's
+    ``uniform_int2_qdq`` output bit for bit, ties to even included."""
+    z = np.load(golden_dir / "uniform.npz")
+    x, deq = z["x"], z["deq"]
+    assert np.array_equal(codec.uniform_qdq(x), deq)
+    codes, scale, mn = codec.encode_uniform(x)
+    ties = codes[24, :8]  # (0, .5, 1.5, 2.5, 3, 1, 2, .25) with scale 1: halves go to even
+    assert list(ties) == [0, 0, 2, 2, 3, 1, 2, 0]
+    assert np.all(scale[26] == 1.0) and np.all(codes[26] == 0)  # constant group
