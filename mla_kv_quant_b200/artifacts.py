@@ -13,7 +13,6 @@ from __future__ import annotations
 import hashlib
 import json
 import os
-import tempfile
 from pathlib import Path
 from typing import Any
 
@@ -26,60 +25,51 @@ CONFIG_FIELDS = ("model_type", "num_hidden_layers", "kv_lora_rank", "qk_rope_hea
 
 
 def sha256_file(path: str | Path) -> str:
-    digest = hashlib.sha256()
-    with Path(path).open("rb") as handle:
-        for chunk in iter(lambda: handle.read(1024 * 1024), b""):
-            digest.update(chunk)
-    return digest.hexdigest()
+    """Hex SHA-256 of a file's bytes (the manifest's per-layer ``sha256``)."""
+    with open(path, "rb") as f:
+        return hashlib.file_digest(f, "sha256").hexdigest()
 
 
-def atomic_write_json(path: str | Path, value) -> None:
-    """Atomically replace a JSON file (``mla_quant/artifacts.py:19-33``)."""
-    path = Path(path)
+def _write_json_replacing(path: Path, value) -> None:
+    """Write ``value`` as indented JSON next to ``path``, then rename it over ``path``
+    (readers never see a half-written manifest)."""
     path.parent.mkdir(parents=True, exist_ok=True)
-    fd, temporary = tempfile.mkstemp(prefix=f".{path.name}.", dir=path.parent)
-    try:
-        with os.fdopen(fd, "w") as handle:
-            json.dump(value, handle, ensure_ascii=False, indent=2, allow_nan=False)
-            handle.write("\n")
-            handle.flush()
-            os.fsync(handle.fileno())
-        os.replace(temporary, path)
-    finally:
-        if os.path.exists(temporary):
-            os.unlink(temporary)
+    staged = path.with_name(f".{path.name}.{os.getpid()}.tmp")
+    staged.write_text(json.dumps(value, ensure_ascii=False, indent=2, allow_nan=False) + "\n")
+    os.replace(staged, path)
 
 
-def checkpoint_identity(model_path: str | Path) -> dict[str, Any]:
-    """Config/index hashes of a local checkpoint (``mla_quant/oscar.py:26-43``)."""
-    root = Path(model_path).expanduser().resolve()
-    config_path = root / "config.json"
-    if not config_path.is_file():
-        raise ValueError(f"OSCAR requires a local model directory with config.json: {root}")
-    config = json.loads(config_path.read_text())
-    index = root / "model.safetensors.index.json"
-    return {
-        "checkpoint_name": root.name,
-        "config_sha256": sha256_file(config_path),
-        "weight_index_sha256": sha256_file(index) if index.exists() else None,
-        **{key: config.get(key) for key in CONFIG_FIELDS},
-    }
-
-
-def local_checkpoint_fingerprint(model_path: str | Path) -> dict:
-    """Identity plus shard sizes (``mla_quant/artifacts.py:43-58``)."""
-    root = Path(model_path).expanduser().resolve()
-    identity = checkpoint_identity(root)
+def _shard_sizes(root: Path) -> dict[str, dict[str, int]]:
+    """{shard file: {"size": bytes}} of a local checkpoint: the shards a safetensors index
+    names, else every ``*.safetensors`` file, else every ``pytorch_model*.bin`` file."""
     index = root / "model.safetensors.index.json"
     if index.is_file():
-        names = sorted(set(json.loads(index.read_text())["weight_map"].values()))
+        shards = set(json.loads(index.read_text())["weight_map"].values())
     else:
-        names = [p.name for p in sorted(root.glob("*.safetensors"))]
-        if not names:
-            names = [p.name for p in sorted(root.glob("pytorch_model*.bin"))]
-    identity["weight_files"] = {name: {"size": (root / name).stat().st_size} for name in names}
-    identity["weight_identity_policy"] = "config_index_sha256_and_shard_size"
-    return identity
+        shards = {p.name for p in root.glob("*.safetensors")} or {p.name for p in root.glob("pytorch_model*.bin")}
+    return {name: {"size": (root / name).stat().st_size} for name in sorted(shards)}
+
+
+def checkpoint_fingerprint(model_path: str | Path) -> dict[str, Any]:
+    """The checkpoint identity a v2 manifest records under ``model`` and that
+    ``LearnedRotationQuantizer.validate_config`` compares (``mla_quant/quantizer.py:
+    266-289``): hashes of ``config.json`` and of the safetensors index (None without
+    one), the shard sizes, and the config fields ``CONFIG_FIELDS``."""
+    root = Path(model_path).expanduser().resolve()
+    config_file = root / "config.json"
+    if not config_file.is_file():
+        raise ValueError(f"OSCAR requires a local model directory with config.json: {root}")
+    index = root / "model.safetensors.index.json"
+    config = json.loads(config_file.read_text())
+    fingerprint: dict[str, Any] = {field: config.get(field) for field in CONFIG_FIELDS}
+    fingerprint.update(
+        checkpoint_name=root.name,
+        config_sha256=sha256_file(config_file),
+        weight_index_sha256=sha256_file(index) if index.exists() else None,
+        weight_files=_shard_sizes(root),
+        weight_identity_policy="config_index_sha256_and_shard_size",
+    )
+    return fingerprint
 
 
 def write_synthetic_artifact(output_dir: str | Path, rotations: dict[int, torch.Tensor],
@@ -114,5 +104,5 @@ def write_synthetic_artifact(output_dir: str | Path, rotations: dict[int, torch.
         "layers": layers,
         "calibration": calibration or {"source": "synthetic"},
     }
-    atomic_write_json(root / "manifest.json", manifest)
+    _write_json_replacing(root / "manifest.json", manifest)
     return manifest

@@ -190,7 +190,7 @@ class LearnedRotationQuantizer:
 
     def validate_config(self, config: Any) -> None:
         """``quantizer.py:266-289``."""
-        from .artifacts import local_checkpoint_fingerprint
+        from .artifacts import checkpoint_fingerprint
         from .numerics import validate_artifact_numerics
 
         validate_artifact_numerics(self.manifest)
@@ -203,7 +203,7 @@ class LearnedRotationQuantizer:
         model_path = getattr(config, "_name_or_path", "")
         if not model_path:
             raise ValueError("learned artifact validation needs the model checkpoint path")
-        actual = local_checkpoint_fingerprint(model_path)
+        actual = checkpoint_fingerprint(model_path)
         identity_fields = ["config_sha256", "weight_index_sha256"]
         if "weight_files" in expected:
             sizes = lambda record: {name: value["size"] for name, value in record.items()}  # noqa: E731

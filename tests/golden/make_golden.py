@@ -11,6 +11,8 @@ it writes; the tests never import the reference.
 
 Fixtures written:
 
+* ``fingerprint.json`` -- ``local_checkpoint_fingerprint`` (``mla_quant/artifacts.py:43-58``)
+  of the fake checkpoint ``make_fake_checkpoint`` builds.
 * ``uniform.npz``   -- ``uniform_int2_qdq`` (``mla_quant/oscar.py:91-101``), OSCAR's
   uniform min/max INT2 baseline, on seeded rows plus exact-tie and constant groups.
 * ``codec.npz``     -- ``oscar_lloyd_int2_qdq`` (``mla_quant/oscar.py:120-144``) on
@@ -76,10 +78,28 @@ def signal_gain(t: float) -> float:
     return 1 / (2 * (inner * (phi0 - phi_t) + outer * phi_t))
 
 
+def make_fake_checkpoint(root: Path) -> Path:
+    """A local checkpoint directory with fixed bytes: config.json, a safetensors index
+    naming two shards, and the shards (sizes are all that the fingerprint reads).  The
+    tests rebuild the same directory with this function."""
+    root.mkdir(parents=True, exist_ok=True)
+    config = {"model_type": "minicpm3", "num_hidden_layers": 2, "kv_lora_rank": 256, "qk_rope_head_dim": 32,
+              "hidden_size": 2560}
+    (root / "config.json").write_text(json.dumps(config, indent=2, sort_keys=True) + "\n")
+    index = {"metadata": {"total_size": 3000},
+             "weight_map": {"a.weight": "model-00001-of-00002.safetensors",
+                            "b.weight": "model-00002-of-00002.safetensors",
+                            "c.weight": "model-00001-of-00002.safetensors"}}
+    (root / "model.safetensors.index.json").write_text(json.dumps(index, indent=2, sort_keys=True) + "\n")
+    (root / "model-00001-of-00002.safetensors").write_bytes(bytes(range(256)) * 7)
+    (root / "model-00002-of-00002.safetensors").write_bytes(b"\x5a" * 1208)
+    return root
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="checkout of noforit/mla_kv_quant")
-    ap.add_argument("--only", choices=["uniform"], default=None, help="write only this fixture")
+    ap.add_argument("--only", choices=["uniform", "fingerprint"], default=None, help="write only this fixture")
     args = ap.parse_args()
     ref = Path(args.reference).resolve()
     sys.path.insert(0, str(ref))
@@ -99,6 +119,20 @@ def main() -> None:
 
     configure_reference_numerics()
     torch.manual_seed(0)
+
+    # ---- checkpoint fingerprint of a fake local checkpoint (mla_quant/artifacts.py:43-58) ----
+    if args.only in (None, "fingerprint"):
+        import tempfile
+
+        from mla_quant.artifacts import local_checkpoint_fingerprint
+
+        with tempfile.TemporaryDirectory() as tmp:
+            ckpt = make_fake_checkpoint(Path(tmp) / "fake-minicpm3")
+            fp = local_checkpoint_fingerprint(ckpt)
+        (HERE / "fingerprint.json").write_text(json.dumps(fp, indent=2, sort_keys=True) + "\n")
+        if args.only == "fingerprint":
+            print("wrote fingerprint.json to", HERE)
+            return
 
     # ---- uniform min/max baseline codec (mla_quant/oscar.py:91-101) ----------------------
     from mla_quant.oscar import uniform_int2_qdq

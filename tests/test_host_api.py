@@ -137,3 +137,39 @@ def test_synth_distributions():
     pt, slots = synth.page_table(3, 130)
     assert pt.shape == (3, 3) and int(pt.min()) >= 1 and slots == (3 * 3 + 1) * 64
     assert len(set(pt.flatten().tolist())) == 9
+
+
+def _fake_checkpoint(tmp_path):
+    import importlib.util
+    from pathlib import Path
+
+    spec = importlib.util.spec_from_file_location("make_golden", Path(__file__).parent / "golden" / "make_golden.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod.make_fake_checkpoint(tmp_path / "fake-minicpm3")
+
+
+def test_checkpoint_fingerprint_matches_reference(golden_dir, tmp_path):
+    from mla_kv_quant_b200.artifacts import checkpoint_fingerprint
+
+    ckpt = _fake_checkpoint(tmp_path)
+    assert checkpoint_fingerprint(ckpt) == json.loads((golden_dir / "fingerprint.json").read_text())
+
+
+def test_validate_config_checks_the_checkpoint(tmp_path):
+    from types import SimpleNamespace
+
+    from mla_kv_quant_b200.artifacts import checkpoint_fingerprint, write_synthetic_artifact
+
+    ckpt = _fake_checkpoint(tmp_path)
+    rots = {i: synth.rotation(256, 60 + i) for i in range(2)}
+    write_synthetic_artifact(tmp_path / "art", rots, {0: (0.8, 1.0), 1: (0.9, 1.1)}, checkpoint_fingerprint(ckpt))
+    q = LearnedRotationQuantizer(tmp_path / "art")
+    cfg = SimpleNamespace(model_type="minicpm3", num_hidden_layers=2, kv_lora_rank=256, qk_rope_head_dim=32,
+                          _name_or_path=str(ckpt))
+    q.validate_config(cfg)
+    with pytest.raises(ValueError, match="model mismatch: kv_lora_rank"):
+        q.validate_config(SimpleNamespace(**dict(vars(cfg), kv_lora_rank=512)))
+    (ckpt / "model-00002-of-00002.safetensors").write_bytes(b"\x00" * 10)
+    with pytest.raises(ValueError, match="shard names/sizes differ"):
+        q.validate_config(SimpleNamespace(**vars(cfg)))
