@@ -9,7 +9,10 @@
   writer's.
 * Decode, config 2: 64 requests x 16384 tokens with the benchmark's default split
   count (9), through the caller-scratch and the static-scratch entry points, a seeded
-  subset of 8 requests against the FP64 oracle (max-abs <= 2e-2, cosine >= 0.9995).
+  subset of 8 requests against the FP64 oracle with the decode tests' tolerance: the
+  kernel's FP32 result (its partials merged in FP32) within max-abs 2e-2, the BF16 output
+  within 2e-2 plus half a BF16 ulp of the value (the output format's own rounding),
+  cosine >= 0.9995; the static-scratch output equals the caller-scratch output.
 """
 
 import numpy as np
@@ -81,8 +84,7 @@ def config2_pool():
     return pool, pt, seq_lens
 
 
-@pytest.mark.parametrize("entry", ["caller_scratch", "static_scratch"])
-def test_decode_config2_default_splits(config2_pool, entry):
+def test_decode_config2_default_splits(config2_pool):
     import ctypes
 
     from mla_kv_quant_b200 import _lib
@@ -98,25 +100,35 @@ def test_decode_config2_default_splits(config2_pool, entry):
     lse = torch.full((b, h), float("nan"), device="cuda")
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     sm = 1.0 / np.sqrt(192.0)
-    if entry == "caller_scratch":
-        part_o = torch.empty(b, h, splits + 1, d, device="cuda")
-        part_lse = torch.empty(b, h, splits + 1, device="cuda")
-        ops.packed_decode(q, pool.view(), pt, sl, sm, splits, part_o, part_lse, out, out_lse=lse, err=err)
-    else:
-        lib = _lib.load()
-        cs = pool.view().c_struct()
-        stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-        rc = lib.rolaq_packed_decode_static(q.data_ptr(), q.stride(0), q.stride(1), b, h, ctypes.byref(cs),
-                                            pt.data_ptr(), pt.stride(0), pt.shape[1], sl.data_ptr(), None, sm, splits,
-                                            out.data_ptr(), out.stride(0), out.stride(1), lse.data_ptr(),
-                                            err.data_ptr(), stream)
-        assert rc == 0, lib.rolaq_last_error()
+    part_o = torch.empty(b, h, splits + 1, d, device="cuda")
+    part_lse = torch.empty(b, h, splits + 1, device="cuda")
+    ops.packed_decode(q, pool.view(), pt, sl, sm, splits, part_o, part_lse, out, out_lse=lse, err=err)
+    o32 = torch.empty(b * h, d, device="cuda")
+    ops.merge_partials(part_o.view(b * h, splits + 1, d).transpose(0, 1), part_lse.view(b * h, splits + 1).t(),
+                       out_f32=o32)
+    # the static-scratch entry point, called through the C ABI, on the same inputs
+    lib = _lib.load()
+    cs = pool.view().c_struct()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    out_s = torch.full_like(out, float("nan"))
+    lse_s = torch.full_like(lse, float("nan"))
+    rc = lib.rolaq_packed_decode_static(q.data_ptr(), q.stride(0), q.stride(1), b, h, ctypes.byref(cs),
+                                        pt.data_ptr(), pt.stride(0), pt.shape[1], sl.data_ptr(), None, sm, splits,
+                                        out_s.data_ptr(), out_s.stride(0), out_s.stride(1), lse_s.data_ptr(),
+                                        err.data_ptr(), stream)
+    assert rc == 0, lib.rolaq_last_error()
     torch.cuda.synchronize()
     assert int(err.item()) == 0
+    assert torch.equal(out_s, out) and torch.equal(lse_s, lse)
     sub = sorted(np.random.default_rng(55).choice(b, size=8, replace=False).tolist())
     ref, ref_lse = odecode.decode(pool.to_oracle(), bits(q), pt.cpu().numpy(), seq_lens, sm, requests=sub)
     o = out.float().cpu().numpy()
+    f = o32.view(b, h, d).cpu().numpy()
     for i in sub:
-        assert np.abs(o[i] - ref[i]).max() <= 2e-2, f"request {i}"
+        e32 = np.abs(f[i] - ref[i]).max()
+        print(f"request {i}: FP32 max-abs {e32:.4g}, max |ref| {np.abs(ref[i]).max():.3g}")
+        assert e32 <= 2e-2, f"request {i}: FP32 max-abs {e32}"
+        half_ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(ref[i]), 1e-30))) - 8)
+        assert np.max(np.abs(o[i] - ref[i]) - half_ulp) <= 2e-2, f"request {i}"
         assert cosine(o[i], ref[i]) >= 0.9995
     assert np.allclose(lse.cpu().numpy()[sub], ref_lse[sub], atol=2e-3)
