@@ -523,7 +523,7 @@ def decode_step_config(dev, layers, heads, d, dr, batch, ctx, sm_scale, steps, w
     res = {"tok_s": world * batch / step_s, "ms_per_step": step_s * 1e3, "steps": steps, "warmup": warmup,
            "layers": layers, "heads": heads, "kv_lora_rank": d, "rope_dim": dr, "batch_per_gpu": batch, "ctx": ctx,
            "sm_scale": sm_scale, "num_splits": splits,
-           "decode_kernel": "decode_tc (tcgen05)" if (d, dr, heads) == (512, 64, 16) else "decode_kernel (warp MMA)",
+           "decode_kernel": f"decode_tc_kernel<{d}, {dr}, {heads}> (tcgen05)",
            "roofline": {"bound": "hbm", "launch_us": dec_s * 1e6, "algorithmic_bytes_per_launch": dbytes,
                         "achieved": dbytes / dec_s / 1e9, "peak": hbm, "unit": "GB/s",
                         "frac": dbytes / dec_s / 1e9 / hbm}}

@@ -251,11 +251,112 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       : "memory");
 }
 
+// 32 lanes x 16 columns -> 16 registers per thread.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+// 32 lanes x 2 columns -> 2 registers per thread.
+__device__ __forceinline__ void tmem_ld2(uint32_t taddr, uint32_t (&r)[2]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(taddr));
+}
+
+// 4 registers per thread -> 32 lanes x 4 columns.
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t (&r)[4]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(r[0]), "r"(r[1]),
+               "r"(r[2]), "r"(r[3])
+               : "memory");
+}
+
+// Shared-memory descriptor for a K-major operand in the canonical 64-byte swizzled layout
+// (CU_TENSOR_MAP_SWIZZLE_64B): rows of 32 BF16 (64 B), 8-row atoms of 512 B, start address
+// advanced by 32 B per K = 16 step inside the row.  Tile base 512-byte aligned.
+__device__ __forceinline__ uint64_t sw64_kmajor_desc(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);  // start address
+  d |= static_cast<uint64_t>(1u) << 16;                     // leading byte offset (unused here)
+  d |= static_cast<uint64_t>(512u >> 4) << 32;              // stride byte offset: 8-row atom
+  d |= static_cast<uint64_t>(1u) << 46;                     // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(4u) << 61;                     // SWIZZLE_64B
+  return d;
+}
+
 // 32 lanes x 4 columns -> 4 registers per thread.
 __device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t (&r)[4]) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(taddr));
+}
+
+// N consecutive TMEM columns (32 lanes) -> r[0..N), as x16 / x8 / x4 / x2 / x1 loads of at most
+// ALIGN columns each (ALIGN: a power of two dividing the start column), so that every load
+// starts at a multiple of its own width.
+template <int N, int ALIGN, int OFF = 0>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t* r) {
+  constexpr int REM = N - OFF;
+  if constexpr (REM >= 16 && ALIGN >= 16) {
+    uint32_t t[16];
+    tmem_ld16(taddr + OFF, t);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) r[OFF + i] = t[i];
+    tmem_ld_cols<N, ALIGN, OFF + 16>(taddr, r);
+  } else if constexpr (REM >= 8 && ALIGN >= 8) {
+    uint32_t t[8];
+    tmem_ld8(taddr + OFF, t);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) r[OFF + i] = t[i];
+    tmem_ld_cols<N, ALIGN, OFF + 8>(taddr, r);
+  } else if constexpr (REM >= 4 && ALIGN >= 4) {
+    uint32_t t[4];
+    tmem_ld4(taddr + OFF, t);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) r[OFF + i] = t[i];
+    tmem_ld_cols<N, ALIGN, OFF + 4>(taddr, r);
+  } else if constexpr (REM >= 2 && ALIGN >= 2) {
+    uint32_t t[2];
+    tmem_ld2(taddr + OFF, t);
+    r[OFF] = t[0];
+    r[OFF + 1] = t[1];
+    tmem_ld_cols<N, ALIGN, OFF + 2>(taddr, r);
+  } else if constexpr (REM >= 1) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r[OFF]) : "r"(taddr + OFF));
+    tmem_ld_cols<N, ALIGN, OFF + 1>(taddr, r);
+  }
+}
+
+// r[0..N) -> N consecutive TMEM columns (32 lanes), as x16 / x8 / x4 stores of at most ALIGN
+// columns each (N and ALIGN multiples of 4).
+template <int N, int ALIGN, int OFF = 0>
+__device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t* r) {
+  constexpr int REM = N - OFF;
+  static_assert(N % 4 == 0 && ALIGN % 4 == 0, "whole x4 groups");
+  if constexpr (REM >= 16 && ALIGN >= 16) {
+    uint32_t t[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) t[i] = r[OFF + i];
+    tmem_st16(taddr + OFF, t);
+    tmem_st_cols<N, ALIGN, OFF + 16>(taddr, r);
+  } else if constexpr (REM >= 8 && ALIGN >= 8) {
+    uint32_t t[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t[i] = r[OFF + i];
+    tmem_st8(taddr + OFF, t);
+    tmem_st_cols<N, ALIGN, OFF + 8>(taddr, r);
+  } else if constexpr (REM >= 4) {
+    uint32_t t[4] = {r[OFF], r[OFF + 1], r[OFF + 2], r[OFF + 3]};
+    tmem_st4(taddr + OFF, t);
+    tmem_st_cols<N, ALIGN, OFF + 4>(taddr, r);
+  }
+}
+
+// The largest power of two (<= 16) dividing n: the column alignment of starts n * k.
+__host__ __device__ constexpr int pow2_align(int n) {
+  return (n % 16 == 0) ? 16 : (n % 8 == 0) ? 8 : (n % 4 == 0) ? 4 : (n % 2 == 0) ? 2 : 1;
 }
 
 // Ties registers written by tcgen05.ld to the preceding tcgen05.wait::ld, so that no

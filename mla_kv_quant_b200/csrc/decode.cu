@@ -1169,15 +1169,16 @@ static int launch_window_t(const DecodeArgs& a, cudaStream_t s) {
 }
 
 bool decode_tc_supported(const DecodeArgs& a, int heads);
-int launch_decode_tc(const DecodeArgs& a, cudaStream_t s);
+int launch_decode_tc(const DecodeArgs& a, int heads, cudaStream_t s);
 
 int launch_decode(const DecodeArgs& a, int heads, cudaStream_t s) {
   const int d = a.cache.latent_dim, dr = a.cache.rope_dim;
   if (decode_tc_supported(a, heads)) {
     // tcgen05 kernel for the INT2 splits, the window split on its own
-    int rc = launch_decode_tc(a, s);
+    int rc = launch_decode_tc(a, heads, s);
     if (rc != ROLAQ_OK) return rc;
-    return launch_window_t<512, 64, 16>(a, s);
+    if (d == 512) return heads == 16 ? launch_window_t<512, 64, 16>(a, s) : launch_window_t<512, 64, 8>(a, s);
+    return heads == 40 ? launch_window_t<256, 32, 40>(a, s) : launch_window_t<256, 32, 16>(a, s);
   }
   if (d == 512 && dr == 64 && heads == 16) return launch_decode_t<512, 64, 16>(a, s);
   if (d == 512 && dr == 64 && heads == 8) return launch_decode_t<512, 64, 8>(a, s);
@@ -1213,7 +1214,7 @@ int launch_merge(const float* part_o, int64_t row_stride, int64_t part_stride, c
 // ROLAQ_EUNSUPPORTED and the caller runs launch_decode + launch_merge.
 int launch_decode_merged(const DecodeArgs& a, int heads, uint16_t* out, int64_t out_sb, int64_t out_sh,
                          float* out_lse, cudaStream_t s) {
-  if (!decode_tc_supported(a, heads)) return ROLAQ_EUNSUPPORTED;
+  if (!decode_tc_supported(a, heads) || a.cache.latent_dim != 512) return ROLAQ_EUNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(out) & 7u) || (out_sb & 3) || (out_sh & 3) ||
       (reinterpret_cast<uintptr_t>(a.part_o) & 15u))
     return ROLAQ_EUNSUPPORTED;
@@ -1224,7 +1225,7 @@ int launch_decode_merged(const DecodeArgs& a, int heads, uint16_t* out, int64_t 
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    kMaxWindow * kMwRowBytes) == cudaSuccess;
   if (!mw_attr) return ROLAQ_ECUDA;
-  int rc = launch_decode_tc(a, s);
+  int rc = launch_decode_tc(a, heads, s);
   if (rc != ROLAQ_OK) return rc;
   // Programmatic dependent launch: the window phase overlaps the tcgen05 kernel's last CTAs;
   // the merge waits for that grid's completion (griddepcontrol.wait) before reading partials.

@@ -292,9 +292,10 @@ def default_num_splits(batch: int, max_ctx: int, sm_count: int = 148, ctas_per_s
                        latent_dim: int = 512, rope_dim: int = 64, heads: int = 16) -> int:
     """Pick the number of INT2 KV splits per request so that ``batch * splits`` CTAs
     fill whole waves of the GPU and each split keeps at least 4 pages.  The tcgen05
-    kernel of the 512/64/16 shape holds one CTA per SM; the warp-MMA kernel two."""
+    kernel (every built shape) holds one CTA per SM."""
     if ctas_per_sm is None:
-        ctas_per_sm = 1 if (latent_dim, rope_dim, heads) == (512, 64, 16) else 2
+        tc = {(512, 64, 16), (512, 64, 8), (256, 32, 40), (256, 32, 16)}
+        ctas_per_sm = 1 if (latent_dim, rope_dim, heads) in tc else 2
     pages = max(1, math.ceil(max_ctx / PAGE))
     slots = sm_count * ctas_per_sm
     best, best_cost = 1, float("inf")

@@ -132,3 +132,40 @@ def test_decode_config2_default_splits(config2_pool):
         assert np.max(np.abs(o[i] - ref[i]) - half_ulp) <= 2e-2, f"request {i}"
         assert cosine(o[i], ref[i]) >= 0.9995
     assert np.allclose(lse.cpu().numpy()[sub], ref_lse[sub], atol=2e-3)
+
+
+def test_decode_minicpm3_shape_default_splits():
+    """The MiniCPM3-4B shape (D = 256, Dr = 32, H = 40, softmax scale 1/sqrt(64 + 32)) on
+    the tcgen05 kernel: 8 requests x 8192 tokens with the default split count, every
+    request against the FP64 oracle."""
+    d, dr, h, b, ctx = 256, 32, 40, 8, 8192
+    seq_lens = [ctx] * b
+    g = torch.Generator().manual_seed(61)
+    pages = ctx // 64
+    pt = (torch.randperm(b * pages, generator=g) + 1).to(torch.int32).reshape(b, pages).cuda()
+    pool = GpuPool(64 * (b * pages + 1), d, dr, max_reqs=b, sink=4, recent=16)
+    fill_requests(pool, seq_lens, pt, synth.rotation(d, seed=62), ops.codec_serving(0.9, synth.signal_gain(0.9)),
+                  seed=63)
+    splits = ops.default_num_splits(b, ctx, latent_dim=d, rope_dim=dr, heads=h)
+    q = synth.normal_bf16((b, h, d + dr), seed=64, device="cuda")
+    sl = torch.tensor(seq_lens, dtype=torch.int32, device="cuda")
+    out = torch.empty(b, h, d, dtype=torch.bfloat16, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    sm = 1.0 / np.sqrt(96.0)
+    part_o = torch.empty(b, h, splits + 1, d, device="cuda")
+    part_lse = torch.empty(b, h, splits + 1, device="cuda")
+    ops.packed_decode(q, pool.view(), pt, sl, sm, splits, part_o, part_lse, out, err=err)
+    o32 = torch.empty(b * h, d, device="cuda")
+    ops.merge_partials(part_o.view(b * h, splits + 1, d).transpose(0, 1), part_lse.view(b * h, splits + 1).t(),
+                       out_f32=o32)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref, _ = odecode.decode(pool.to_oracle(), bits(q), pt.cpu().numpy(), seq_lens, sm)
+    o = out.float().cpu().numpy()
+    f = o32.view(b, h, d).cpu().numpy()
+    for i in range(b):
+        assert np.abs(f[i] - ref[i]).max() <= 2e-2, f"request {i}"
+        half_ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(ref[i]), 1e-30))) - 8)
+        assert np.max(np.abs(o[i] - ref[i]) - half_ulp) <= 2e-2, f"request {i}"
+        assert cosine(o[i], ref[i]) >= 0.9995
+

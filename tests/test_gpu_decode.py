@@ -84,10 +84,10 @@ def test_decode_matches_oracle(d, dr, h, splits):
 
 
 @pytest.mark.parametrize("direction", ["rising", "falling"])
-def test_decode_drifting_scales_and_scores(direction):
+@pytest.mark.parametrize("d,dr,h", [(512, 64, 16), (256, 32, 40)])
+def test_decode_drifting_scales_and_scores(direction, d, dr, h):
     """Group scales and scores that drift 2^6 along the sequence: the kernel's running
     reference max and per-group weight scale both move many times inside a split."""
-    d, dr, h = 512, 64, 16
     seq_lens = [3000, 2200]
 
     def gain(L):
