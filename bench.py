@@ -368,6 +368,13 @@ def run_ours(args, rank, world, dev):
     h2d = LAYERS * (q[0].numel() * 2 + new_ckv[0].numel() * 2 + new_pe[0].numel() * 2)
     d2h = LAYERS * out[0].numel() * 2
 
+    # e2e of the absorbed layer: the same step starting from q_nope / q_pe and ending at the
+    # projected output (rolaq_sglang.patch:205-248): per layer absorb_query (q_nope W_kc' and
+    # the q_pe concat), the fused writer, the packed decode, project_output (o W_vc'); inputs
+    # copied up and the projected outputs copied down inside the timed region, graph-replayed.
+    e2e_abs = e2e_absorbed(args, world, dev, pool, pt, seq, req, loc, splits, sm_scale, new_ckv, new_pe, part_o,
+                           part_lse)
+
     # writer leg (config 1), rank-local
     wrows, w_s = time_writer(pool, dev, ctx, warmup=2, iters=max(3, min(10, args.steps // 20)))
     w_bytes = writer_bytes(wrows)
@@ -403,7 +410,8 @@ def run_ours(args, rank, world, dev):
                         "overlapped with the layers on two copy streams, the whole step (copies included) replayed "
                         "from a CUDA graph as a serving engine captures its decode step",
                 "eager": {"value": world * batch / e2e_eager_s, "unit": "tok/s", "ms_per_step": e2e_eager_s * 1e3,
-                          "path": "the same calls and copies launched eagerly every step"}},
+                          "path": "the same calls and copies launched eagerly every step"},
+                "absorbed": e2e_abs},
         "roofline": {"kernel": "rolaq decode (decode_tc_kernel + merge_window_kernel), one layer", "bound": "hbm",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_source": f"{peak_kind} hbm_gbs", "traffic": traffic, "traffic_source": traffic_src,
@@ -415,7 +423,7 @@ def run_ours(args, rank, world, dev):
                    "bound": "tensor" if w_flops / (tf_burst * 1e12) > w_bytes / (hbm * 1e9) else "hbm",
                    "note": "roofline_frac = max(bytes/HBM peak, flops/bf16 peak) / time, of " + peak_kind},
         "clocks": clocks,
-        "gpu_launches": args.steps * LAYERS * 3,
+        "gpu_launches": args.steps * LAYERS * 3,  # per layer: fused writer, decode_tc, merge_window
         "gpus_active": world,
     }
     return res
@@ -545,6 +553,78 @@ def run_batch4a(args, rank, world, dev):
     return {"mode": "batch4a", "metric": "INT2 MLA decode tok/s, B512 x 32K ctx, request-sharded", "n_gpus": world,
             "gpus_active": world, "value": r["tok_s"], "unit": "tok/s", "scaling": "strong",
             "global_batch": total, **{k: v for k, v in r.items() if k != "tok_s"}}
+
+
+def e2e_absorbed(args, world, dev, pool, pt, seq, req, loc, splits, sm_scale, new_ckv, new_pe, part_o, part_lse,
+                 qk_nope=128, v_head=128):
+    """The decode step from the per-head q_nope / q_pe to the projected attention output:
+    absorb_query -> try_fast_decode_store -> packed_mla_decode_gf_fwd -> project_output per
+    layer, with seeded BF16 kv_b_proj weights in SGLang's bmm layouts."""
+    from mla_kv_quant_b200 import absorbed, synth
+    from mla_kv_quant_b200.mla_fused_writer import try_fast_decode_store
+    from mla_kv_quant_b200.mla_packed_decode import packed_mla_decode_gf_fwd
+
+    batch = seq.numel()
+    w_kc, w_vc = [], []
+    for li in range(LAYERS):
+        w = (synth.normal_bf16((HEADS * (qk_nope + v_head), D), 300 + li, dev).float() * 0.05).to(torch.bfloat16)
+        a, b = absorbed.split_absorbed_weights(w, HEADS, qk_nope, v_head)
+        w_kc.append(a)
+        w_vc.append(b)
+    h_qn = synth.normal_bf16((LAYERS, batch, HEADS, qk_nope), 21, dev).cpu().pin_memory()
+    h_qp = synth.normal_bf16((LAYERS, batch, HEADS, DR), 22, dev).cpu().pin_memory()
+    h_ckv, h_pe = new_ckv.cpu().pin_memory(), new_pe.cpu().pin_memory()
+    h_y = torch.empty(LAYERS, batch, HEADS, v_head, dtype=torch.bfloat16).pin_memory()
+    d_qn = torch.empty(LAYERS, batch, HEADS, qk_nope, dtype=torch.bfloat16, device=dev)
+    d_qp = torch.empty(LAYERS, batch, HEADS, DR, dtype=torch.bfloat16, device=dev)
+    d_ckv, d_pe = torch.empty_like(new_ckv), torch.empty_like(new_pe)
+    q = torch.empty(batch, HEADS, D + DR, dtype=torch.bfloat16, device=dev)
+    o = torch.empty(batch, HEADS, D, dtype=torch.bfloat16, device=dev)
+    y = torch.empty(LAYERS, batch, HEADS, v_head, dtype=torch.bfloat16, device=dev)
+    pool.set_window_meta(True, seq, req)
+
+    def step():
+        d_qn.copy_(h_qn, non_blocking=True)
+        d_qp.copy_(h_qp, non_blocking=True)
+        d_ckv.copy_(h_ckv, non_blocking=True)
+        d_pe.copy_(h_pe, non_blocking=True)
+        for li in range(LAYERS):
+            absorbed.absorb_query(d_qn[li], d_qp[li], w_kc[li], out=q)
+            if not try_fast_decode_store(pool, li, loc, d_ckv[li], d_pe[li]):
+                raise RuntimeError("fused decode writer declined a decode step")
+            packed_mla_decode_gf_fwd(q, pool, li, pt, seq, sm_scale, splits, attn_logits=part_o, attn_lse=part_lse,
+                                     out=o)
+            absorbed.project_output(o, w_vc[li], out=y[li])
+        h_y.copy_(y, non_blocking=True)
+
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(args.steps):
+        graph.replay()
+    s1.record()
+    torch.cuda.synchronize()
+    t = max_over_ranks(s0.elapsed_time(s1) / 1e3 / args.steps, world, dev)
+    del graph
+    h2d = (h_qn.numel() + h_qp.numel() + h_ckv.numel() + h_pe.numel()) * 2
+    return {"value": world * batch / t, "unit": "tok/s", "ms_per_step": t * 1e3, "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": h_y.numel() * 2,
+            "path": "per layer absorb_query (q_nope W_kc' + q_pe concat, tcgen05) -> try_fast_decode_store -> "
+                    "packed_mla_decode_gf_fwd -> project_output (o W_vc', tcgen05); copies in and out inside the "
+                    "timed region; whole step graph-replayed"}
 
 
 def max_over_ranks(x, world, dev):

@@ -215,6 +215,39 @@ int rolaq_packed_decode_static(const uint16_t* q, int64_t q_stride_b, int64_t q_
                                int32_t* err, cudaStream_t stream);
 
 /*
+ * Absorbed query of the MLA decode, on tcgen05: per request b and head h,
+ *   q_out[b][h][n]              = sum_k q_nope[b][h][k] * w_kc[h][n][k]   (n < latent_dim)
+ *   q_out[b][h][latent_dim + r] = q_pe[b][h][r]                          (r < rope_dim)
+ * BF16 in, FP32 accumulation, BF16 out: the decode's query [B, H, D + Dr] in the rotated
+ * frame when w_kc has the read rotation folded in.  Replaces torch.bmm(q_nope, w_kc) and the
+ * cat with q_pe of the DeepSeek MLA forward (deployment/patches/rolaq_sglang.patch:205-248,
+ * with w_kc from fold_read_rotation, deployment/sglang/srt/mem_cache/rolaq_mla.py:56-71).
+ *   q_nope  bf16 [B, H, nope_dim] with strides (qn_stride_b, qn_stride_h); nope_dim % 64 == 0
+ *   w_kc    bf16 [H, latent_dim, nope_dim] contiguous (SGLang's storage of w_kc)
+ *   q_pe    bf16 [B, H, rope_dim] or NULL when rope_dim == 0
+ *   q_out   bf16 [B, H, latent_dim + rope_dim] with strides (q_stride_b, q_stride_h)
+ */
+int rolaq_absorb_query(const uint16_t* q_nope, int64_t qn_stride_b, int64_t qn_stride_h, const uint16_t* q_pe,
+                       int64_t qp_stride_b, int64_t qp_stride_h, const uint16_t* w_kc, int32_t batch, int32_t heads,
+                       int32_t nope_dim, int32_t latent_dim, int32_t rope_dim, uint16_t* q_out, int64_t q_stride_b,
+                       int64_t q_stride_h, int32_t* err, cudaStream_t stream);
+
+/*
+ * Output projection after the MLA decode, on tcgen05: per request b and head h,
+ *   out[b][h][v] = sum_e o[b][h][e] * w_vc[h][v][e]
+ * BF16 in, FP32 accumulation, BF16 out; with the read rotation folded into w_vc the decode's
+ * rotated-frame output needs no un-rotation.  Replaces torch.bmm(attn_output, w_vc)
+ * (deployment/patches/rolaq_sglang.patch:261-274 with rolaq_mla.py:56-71).
+ *   o     bf16 [B, H, latent_dim] with strides (o_stride_b, o_stride_h)
+ *   w_vc  bf16 [H, v_dim, latent_dim] contiguous (SGLang's storage of w_vc); v_dim in
+ *         {64, 128, 256, 512}
+ *   out   bf16 [B, H, v_dim] with strides (out_stride_b, out_stride_h)
+ */
+int rolaq_project_output(const uint16_t* o, int64_t o_stride_b, int64_t o_stride_h, const uint16_t* w_vc,
+                         int32_t batch, int32_t heads, int32_t latent_dim, int32_t v_dim, uint16_t* out,
+                         int64_t out_stride_b, int64_t out_stride_h, int32_t* err, cudaStream_t stream);
+
+/*
  * LSE merge of normalised partials: for each row r in [0, rows) and part p in
  * [0, n_parts): o = part_o + r*row_stride + p*part_stride (D floats),
  * lse = part_lse[r*lse_row_stride + p*lse_part_stride] (natural log, -inf = empty).

@@ -42,6 +42,8 @@ EXPORTS = (
     "rolaq_packed_decode_static_capacity",
     "rolaq_packed_decode_static",
     "rolaq_merge_partials",
+    "rolaq_absorb_query",
+    "rolaq_project_output",
 )
 
 
@@ -114,6 +116,8 @@ _SIGS = {
         [P, I64, I64, I32, I32, ctypes.POINTER(LayerCache), P, I64, I32, P, P, F32, I32, P, I64, I64, P, P, P],
     ),
     "rolaq_merge_partials": (INT, [P, I64, I64, P, I64, I64, I32, I64, I32, P, P, I64, P, P]),
+    "rolaq_absorb_query": (INT, [P, I64, I64, P, I64, I64, P, I32, I32, I32, I32, I32, P, I64, I64, P, P]),
+    "rolaq_project_output": (INT, [P, I64, I64, P, I32, I32, I32, I32, P, I64, I64, P, P]),
 }
 
 

@@ -290,6 +290,48 @@ int rolaq_merge_partials(const float* part_o, int64_t row_stride, int64_t part_s
                  "merge");
 }
 
+int rolaq_absorb_query(const uint16_t* q_nope, int64_t qn_stride_b, int64_t qn_stride_h, const uint16_t* q_pe,
+                       int64_t qp_stride_b, int64_t qp_stride_h, const uint16_t* w_kc, int32_t batch, int32_t heads,
+                       int32_t nope_dim, int32_t latent_dim, int32_t rope_dim, uint16_t* q_out, int64_t q_stride_b,
+                       int64_t q_stride_h, int32_t* err, cudaStream_t stream) {
+  if (batch < 0 || heads <= 0) return fail(ROLAQ_EINVAL, "batch must be >= 0 and heads > 0");
+  if (batch == 0) return ROLAQ_OK;
+  if (!q_nope || !w_kc || !q_out) return fail(ROLAQ_EINVAL, "q_nope, w_kc and q_out must be non-NULL");
+  if (nope_dim <= 0 || nope_dim % 64 != 0 || nope_dim > 1024)
+    return fail(ROLAQ_EUNSUPPORTED, "nope_dim %d must be a positive multiple of 64 (<= 1024)", nope_dim);
+  if (latent_dim != 256 && latent_dim != 512)
+    return fail(ROLAQ_EUNSUPPORTED, "latent_dim %d unsupported (256 or 512)", latent_dim);
+  if (rope_dim < 0 || rope_dim % 8 != 0 || (rope_dim > 0 && !q_pe))
+    return fail(ROLAQ_EINVAL, "rope_dim must be a multiple of 8, with q_pe when > 0");
+  if (!aligned16(q_nope) || !aligned16(w_kc) || !aligned16(q_out) || (q_pe && !aligned16(q_pe)))
+    return fail(ROLAQ_EINVAL, "q_nope, q_pe, w_kc and q_out must be 16-byte aligned");
+  if (qn_stride_b % 8 || qn_stride_h % 8 || q_stride_b % 8 || q_stride_h % 8 ||
+      (rope_dim > 0 && (qp_stride_b % 8 || qp_stride_h % 8)))
+    return fail(ROLAQ_EINVAL, "row strides must be multiples of 8 elements");
+  ProjArgs a{q_nope, qn_stride_b, qn_stride_h, w_kc, q_out, q_stride_b, q_stride_h,
+             rope_dim > 0 ? q_pe : nullptr, qp_stride_b, qp_stride_h, rope_dim, batch, heads, latent_dim, nope_dim, err};
+  return cuda_rc(launch_proj(a, stream), "absorb_query");
+}
+
+int rolaq_project_output(const uint16_t* o, int64_t o_stride_b, int64_t o_stride_h, const uint16_t* w_vc,
+                         int32_t batch, int32_t heads, int32_t latent_dim, int32_t v_dim, uint16_t* out,
+                         int64_t out_stride_b, int64_t out_stride_h, int32_t* err, cudaStream_t stream) {
+  if (batch < 0 || heads <= 0) return fail(ROLAQ_EINVAL, "batch must be >= 0 and heads > 0");
+  if (batch == 0) return ROLAQ_OK;
+  if (!o || !w_vc || !out) return fail(ROLAQ_EINVAL, "o, w_vc and out must be non-NULL");
+  if (latent_dim != 256 && latent_dim != 512)
+    return fail(ROLAQ_EUNSUPPORTED, "latent_dim %d unsupported (256 or 512)", latent_dim);
+  if (v_dim != 64 && v_dim != 128 && v_dim != 256 && v_dim != 512)
+    return fail(ROLAQ_EUNSUPPORTED, "v_dim %d unsupported (64, 128, 256 or 512)", v_dim);
+  if (!aligned16(o) || !aligned16(w_vc) || !aligned16(out))
+    return fail(ROLAQ_EINVAL, "o, w_vc and out must be 16-byte aligned");
+  if (o_stride_b % 8 || o_stride_h % 8 || out_stride_b % 8 || out_stride_h % 8)
+    return fail(ROLAQ_EINVAL, "row strides must be multiples of 8 elements");
+  ProjArgs a{o, o_stride_b, o_stride_h, w_vc, out, out_stride_b, out_stride_h, nullptr, 0, 0, 0,
+             batch, heads, v_dim, latent_dim, err};
+  return cuda_rc(launch_proj(a, stream), "project_output");
+}
+
 }  // extern "C"
 
 // ---- rolaq_packed_decode_static: the split partials in a fixed device array --------------------

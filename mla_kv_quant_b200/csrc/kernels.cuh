@@ -47,6 +47,21 @@ struct DecodeArgs {
   int32_t* err;
 };
 
+// Per-head projection GEMM around the decode (proj.cu): out[b, h, :n] = x[b, h, :k] w[h]^T,
+// w[h] = [n, k] row-major; optionally out[b, h, n : n + dr] = pe[b, h, :dr].
+struct ProjArgs {
+  const uint16_t* x;
+  int64_t x_sb, x_sh;
+  const uint16_t* w;
+  uint16_t* out;
+  int64_t o_sb, o_sh;
+  const uint16_t* pe;
+  int64_t pe_sb, pe_sh;
+  int32_t dr;
+  int32_t batch, heads, n, k;
+  int32_t* err;
+};
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -70,6 +85,9 @@ int launch_dequant(const uint8_t* codes, const float* params, const void* slots,
                    int64_t num_slots, float* out_f32, uint16_t* out_bf16, int64_t ld_out, int32_t* err,
                    cudaStream_t s);
 int launch_prepare_splits(const int32_t* splits, int32_t* quant, int32_t* merge, int64_t n, cudaStream_t s);
+
+// proj.cu
+int launch_proj(const ProjArgs& a, cudaStream_t s);
 
 // decode.cu
 int launch_decode(const DecodeArgs& a, int heads, cudaStream_t s);

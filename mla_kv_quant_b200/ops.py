@@ -309,3 +309,44 @@ def default_num_splits(batch: int, max_ctx: int, sm_count: int = 148, ctas_per_s
         if cost < best_cost:
             best, best_cost = s, cost
     return best
+
+
+def absorb_query(q_nope: torch.Tensor, q_pe: torch.Tensor | None, w_kc: torch.Tensor, q_out: torch.Tensor,
+                 err: torch.Tensor | None = None) -> None:
+    """``rolaq_absorb_query``: ``q_out[..., :D] = q_nope @ w_kc[h]^T`` per head, ``q_out[..., D:] = q_pe``.
+
+    q_nope ``[B, H, Dn]``, q_pe ``[B, H, Dr]`` (or None), w_kc ``[H, D, Dn]`` contiguous,
+    q_out ``[B, H, D + Dr]``; all BF16 with contiguous rows."""
+    _check(q_nope, "q_nope", torch.bfloat16, 3)
+    _check(w_kc, "w_kc", torch.bfloat16, 3)
+    _check(q_out, "q_out", torch.bfloat16, 3)
+    b, h, dn = q_nope.shape
+    hh, d, dn2 = w_kc.shape
+    if hh != h or dn2 != dn or not w_kc.is_contiguous():
+        raise ValueError("w_kc must be contiguous [H, D, Dn]")
+    dr = 0 if q_pe is None else q_pe.shape[2]
+    if q_pe is not None:
+        _check(q_pe, "q_pe", torch.bfloat16, 3)
+        if tuple(q_pe.shape[:2]) != (b, h) or q_pe.stride(2) != 1:
+            raise ValueError("q_pe must be [B, H, Dr] with contiguous rows")
+    if tuple(q_out.shape) != (b, h, d + dr) or q_out.stride(2) != 1 or q_nope.stride(2) != 1:
+        raise ValueError("q_out must be [B, H, D + Dr]; rows contiguous")
+    _lib.call("rolaq_absorb_query", q_nope.data_ptr(), q_nope.stride(0), q_nope.stride(1), _lib.ptr(q_pe),
+              0 if q_pe is None else q_pe.stride(0), 0 if q_pe is None else q_pe.stride(1), w_kc.data_ptr(), b, h, dn,
+              d, dr, q_out.data_ptr(), q_out.stride(0), q_out.stride(1), _err_ptr(err), _lib.stream_ptr())
+
+
+def project_output(o: torch.Tensor, w_vc: torch.Tensor, out: torch.Tensor, err: torch.Tensor | None = None) -> None:
+    """``rolaq_project_output``: ``out[b, h] = o[b, h] @ w_vc[h]^T``; o ``[B, H, D]``, w_vc ``[H, Dv, D]``
+    contiguous, out ``[B, H, Dv]``; BF16, contiguous rows."""
+    _check(o, "o", torch.bfloat16, 3)
+    _check(w_vc, "w_vc", torch.bfloat16, 3)
+    _check(out, "out", torch.bfloat16, 3)
+    b, h, d = o.shape
+    hh, dv, d2 = w_vc.shape
+    if hh != h or d2 != d or not w_vc.is_contiguous():
+        raise ValueError("w_vc must be contiguous [H, Dv, D]")
+    if tuple(out.shape) != (b, h, dv) or out.stride(2) != 1 or o.stride(2) != 1:
+        raise ValueError("out must be [B, H, Dv]; rows contiguous")
+    _lib.call("rolaq_project_output", o.data_ptr(), o.stride(0), o.stride(1), w_vc.data_ptr(), b, h, d, dv,
+              out.data_ptr(), out.stride(0), out.stride(1), _err_ptr(err), _lib.stream_ptr())
