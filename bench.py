@@ -575,27 +575,53 @@ def e2e_absorbed(args, world, dev, pool, pt, seq, req, loc, splits, sm_scale, ne
     h_qp = synth.normal_bf16((LAYERS, batch, HEADS, DR), 22, dev).cpu().pin_memory()
     h_ckv, h_pe = new_ckv.cpu().pin_memory(), new_pe.cpu().pin_memory()
     h_y = torch.empty(LAYERS, batch, HEADS, v_head, dtype=torch.bfloat16).pin_memory()
-    d_qn = torch.empty(LAYERS, batch, HEADS, qk_nope, dtype=torch.bfloat16, device=dev)
-    d_qp = torch.empty(LAYERS, batch, HEADS, DR, dtype=torch.bfloat16, device=dev)
-    d_ckv, d_pe = torch.empty_like(new_ckv), torch.empty_like(new_pe)
+    # double-buffered per-layer inputs, as the plain e2e leg: layer l+1's inputs go up on a
+    # copy stream while layer l runs, layer l's projected output comes down on another
+    d_qn = [torch.empty(batch, HEADS, qk_nope, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    d_qp = [torch.empty(batch, HEADS, DR, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    d_ckv = [torch.empty_like(new_ckv[0]) for _ in range(2)]
+    d_pe = [torch.empty_like(new_pe[0]) for _ in range(2)]
     q = torch.empty(batch, HEADS, D + DR, dtype=torch.bfloat16, device=dev)
     o = torch.empty(batch, HEADS, D, dtype=torch.bfloat16, device=dev)
     y = torch.empty(LAYERS, batch, HEADS, v_head, dtype=torch.bfloat16, device=dev)
     pool.set_window_meta(True, seq, req)
+    up, down = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    ev_in = [torch.cuda.Event() for _ in range(LAYERS)]
+    ev_done = [torch.cuda.Event() for _ in range(LAYERS)]
 
     def step():
-        d_qn.copy_(h_qn, non_blocking=True)
-        d_qp.copy_(h_qp, non_blocking=True)
-        d_ckv.copy_(h_ckv, non_blocking=True)
-        d_pe.copy_(h_pe, non_blocking=True)
+        main = torch.cuda.current_stream(dev)
+        up.wait_stream(main)
+
+        def h2d(li):
+            bi = li & 1
+            with torch.cuda.stream(up):
+                if li >= 2:
+                    up.wait_event(ev_done[li - 2])
+                d_qn[bi].copy_(h_qn[li], non_blocking=True)
+                d_qp[bi].copy_(h_qp[li], non_blocking=True)
+                d_ckv[bi].copy_(h_ckv[li], non_blocking=True)
+                d_pe[bi].copy_(h_pe[li], non_blocking=True)
+                ev_in[li].record(up)
+
+        h2d(0)
         for li in range(LAYERS):
-            absorbed.absorb_query(d_qn[li], d_qp[li], w_kc[li], out=q)
-            if not try_fast_decode_store(pool, li, loc, d_ckv[li], d_pe[li]):
+            if li + 1 < LAYERS:
+                h2d(li + 1)
+            bi = li & 1
+            main.wait_event(ev_in[li])
+            absorbed.absorb_query(d_qn[bi], d_qp[bi], w_kc[li], out=q)
+            if not try_fast_decode_store(pool, li, loc, d_ckv[bi], d_pe[bi]):
                 raise RuntimeError("fused decode writer declined a decode step")
             packed_mla_decode_gf_fwd(q, pool, li, pt, seq, sm_scale, splits, attn_logits=part_o, attn_lse=part_lse,
                                      out=o)
             absorbed.project_output(o, w_vc[li], out=y[li])
-        h_y.copy_(y, non_blocking=True)
+            ev_done[li].record(main)
+            with torch.cuda.stream(down):
+                down.wait_event(ev_done[li])
+                h_y[li].copy_(y[li], non_blocking=True)
+        main.wait_stream(up)
+        main.wait_stream(down)
 
     side = torch.cuda.Stream(device=dev)
     side.wait_stream(torch.cuda.current_stream())
@@ -873,11 +899,13 @@ def run_seqsplit(args, rank, world, dev):
     part_lse = torch.empty(1, HEADS, parts, device=dev)
     scratch = torch.empty(1, HEADS, D, dtype=torch.bfloat16, device=dev)
     lse_loc = torch.empty(HEADS, device=dev)
-    o_loc = scratch.view(HEADS, D)
+    o_loc = torch.empty(HEADS, D, device=dev)
     sm = 1.0 / math.sqrt(192.0)
 
-    def layer():  # the slice's merged output (BF16) and LSE, as SequenceSplitDecoder.local_partial
-        ops.packed_decode(q, view, pt, sl, sm, splits, part_o, part_lse, scratch, out_lse=lse_loc, token_range=rng)
+    def layer():  # the slice's FP32 partial and LSE, as SequenceSplitDecoder.local_partial
+        ops.packed_decode(q, view, pt, sl, sm, splits, part_o, part_lse, scratch, token_range=rng)
+        ops.merge_partials(part_o.view(HEADS, parts, D).transpose(0, 1), part_lse.view(HEADS, parts).t(),
+                           out_f32=o_loc, out_lse=lse_loc)
 
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     kern, coll = [], []
@@ -935,7 +963,7 @@ def run_seqsplit(args, rank, world, dev):
             "num_splits_per_rank": splits, "us_per_layer": float(t[2]), "kernel_us": float(t[0]),
             "gather_merge_us": float(t[1]), "us_per_layer_graph": float(t[3]),
             "note": "median over steps of each rank, max over ranks; kernel = the slice's decode call (INT2 "
-                    "splits + window + merge to one BF16 partial and its LSE), gather_merge = one NCCL "
+                    "splits + window + merge) and its FP32 partial merge, gather_merge = one NCCL "
                     "all-gather of the (o, lse) partials + the merge kernel (eager launches); "
                     "us_per_layer_graph = the same layer replayed from a CUDA graph"}
 

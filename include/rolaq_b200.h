@@ -215,6 +215,24 @@ int rolaq_packed_decode_static(const uint16_t* q, int64_t q_stride_b, int64_t q_
                                int32_t* err, cudaStream_t stream);
 
 /*
+ * The reader's page table from SGLang's token -> slot map, in one launch (capture-safe):
+ * page_table[b][p] = req_to_token[req_pool_indices[b]][64 p] / 64 for p < ceil(seq_lens[b] / 64)
+ * when those tokens sit in 64 consecutive slots starting at a multiple of 64, else -1 with
+ * ROLAQ_DEV_BAD_PAGE in *err; pages past the request are -1.  seq_lens_out (int32 [B], may be
+ * NULL) receives the lengths as the reader takes them.  Replaces the request -> token
+ * indexing that TritonAttnBackend.forward_decode hands to packed_mla_decode_gf_fwd
+ * (deployment/patches/rolaq_sglang.patch:51-72; forward_batch.req_to_token_pool.req_to_token,
+ * req_pool_indices, seq_lens).
+ *   req_to_token      int32 [max_reqs, rt_stride], rt_stride >= 64 * max_pages
+ *   req_pool_indices  int32 or int64 [B];  seq_lens int32 or int64 [B]
+ *   page_table        int32 [B, pt_stride], pt_stride >= max_pages
+ */
+int rolaq_page_table_from_req_to_token(const int32_t* req_to_token, int64_t rt_stride, const void* req_pool_indices,
+                                       int req_is64, const void* seq_lens, int seq_lens_is64, int64_t batch,
+                                       int32_t max_pages, int32_t* page_table, int64_t pt_stride,
+                                       int32_t* seq_lens_out, int32_t* err, cudaStream_t stream);
+
+/*
  * Absorbed query of the MLA decode, on tcgen05: per request b and head h,
  *   q_out[b][h][n]              = sum_k q_nope[b][h][k] * w_kc[h][n][k]   (n < latent_dim)
  *   q_out[b][h][latent_dim + r] = q_pe[b][h][r]                          (r < rope_dim)

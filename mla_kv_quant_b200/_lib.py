@@ -44,6 +44,7 @@ EXPORTS = (
     "rolaq_merge_partials",
     "rolaq_absorb_query",
     "rolaq_project_output",
+    "rolaq_page_table_from_req_to_token",
 )
 
 
@@ -116,6 +117,7 @@ _SIGS = {
         [P, I64, I64, I32, I32, ctypes.POINTER(LayerCache), P, I64, I32, P, P, F32, I32, P, I64, I64, P, P, P],
     ),
     "rolaq_merge_partials": (INT, [P, I64, I64, P, I64, I64, I32, I64, I32, P, P, I64, P, P]),
+    "rolaq_page_table_from_req_to_token": (INT, [P, I64, P, INT, P, INT, I64, I32, P, I64, P, P, P]),
     "rolaq_absorb_query": (INT, [P, I64, I64, P, I64, I64, P, I32, I32, I32, I32, I32, P, I64, I64, P, P]),
     "rolaq_project_output": (INT, [P, I64, I64, P, I32, I32, I32, I32, P, I64, I64, P, P]),
 }

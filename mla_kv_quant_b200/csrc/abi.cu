@@ -290,6 +290,22 @@ int rolaq_merge_partials(const float* part_o, int64_t row_stride, int64_t part_s
                  "merge");
 }
 
+int rolaq_page_table_from_req_to_token(const int32_t* req_to_token, int64_t rt_stride, const void* req_pool_indices,
+                                       int req_is64, const void* seq_lens, int seq_lens_is64, int64_t batch,
+                                       int32_t max_pages, int32_t* page_table, int64_t pt_stride,
+                                       int32_t* seq_lens_out, int32_t* err, cudaStream_t stream) {
+  if (batch < 0 || max_pages < 0) return fail(ROLAQ_EINVAL, "batch and max_pages must be >= 0");
+  if (batch == 0 || max_pages == 0) return ROLAQ_OK;
+  if (!req_to_token || !req_pool_indices || !seq_lens || !page_table)
+    return fail(ROLAQ_EINVAL, "req_to_token, req_pool_indices, seq_lens and page_table must be non-NULL");
+  if (rt_stride < int64_t(max_pages) * 64 || pt_stride < max_pages)
+    return fail(ROLAQ_EINVAL, "req_to_token rows must hold max_pages * 64 tokens and page_table rows max_pages");
+  if (batch > 65535) return fail(ROLAQ_EUNSUPPORTED, "batch %lld > 65535", (long long)batch);
+  return cuda_rc(launch_page_table(req_to_token, rt_stride, req_pool_indices, req_is64, seq_lens, seq_lens_is64,
+                                   batch, max_pages, page_table, pt_stride, seq_lens_out, err, stream),
+                 "page_table_from_req_to_token");
+}
+
 int rolaq_absorb_query(const uint16_t* q_nope, int64_t qn_stride_b, int64_t qn_stride_h, const uint16_t* q_pe,
                        int64_t qp_stride_b, int64_t qp_stride_h, const uint16_t* w_kc, int32_t batch, int32_t heads,
                        int32_t nope_dim, int32_t latent_dim, int32_t rope_dim, uint16_t* q_out, int64_t q_stride_b,

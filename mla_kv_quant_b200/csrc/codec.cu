@@ -177,6 +177,41 @@ __global__ void prepare_splits_kernel(const int32_t* __restrict__ splits, int32_
   merge[i] = q + 1;
 }
 
+// Page table of the packed reader from SGLang's token -> slot map: one warp per (request,
+// 64-token page).  Page p of request b is req_to_token[req[b]][64 p] / 64 when the page's
+// tokens sit in 64 consecutive slots starting at a multiple of 64 (the packed pool hands out
+// whole pages); otherwise the page is -1 and ROLAQ_DEV_BAD_PAGE is reported (the reader then
+// skips it).  Pages past the request's length are -1.  The request lengths are copied to
+// int32 alongside, the reader's seq_lens.
+__global__ void page_table_kernel(const int32_t* __restrict__ req_to_token, int64_t rt_stride, const void* req_idx,
+                                  int req64, const void* seq_lens, int seq64, int64_t batch, int32_t max_pages,
+                                  int32_t* __restrict__ page_table, int64_t pt_stride, int32_t* __restrict__ seq_out,
+                                  int32_t* err) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t b = blockIdx.y;
+  const int p = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (b >= batch || p >= max_pages) return;
+  const int64_t req = load_index(req_idx, req64, b);
+  const int64_t L = load_index(seq_lens, seq64, b);
+  if (p == 0 && lane == 0 && seq_out != nullptr) seq_out[b] = static_cast<int32_t>(L);
+  int32_t page = -1;
+  const int64_t t0 = static_cast<int64_t>(p) * 64;
+  if (req >= 0 && t0 < L) {
+    const int32_t* row = req_to_token + req * rt_stride + t0;
+    const int32_t s0 = row[0];
+    const int n = static_cast<int>(L - t0 < 64 ? L - t0 : 64);
+    bool ok = s0 >= 0 && (s0 & 63) == 0;
+    for (int j = lane; j < n; j += 32) ok = ok && row[j] == s0 + j;
+    ok = __all_sync(0xFFFFFFFFu, ok);
+    if (ok) {
+      page = s0 >> 6;
+    } else if (lane == 0) {
+      report(err, ROLAQ_DEV_BAD_PAGE);
+    }
+  }
+  if (lane == 0) page_table[b * pt_stride + p] = page;
+}
+
 static inline unsigned blocks_for(int64_t units, int threads) {
   return static_cast<unsigned>((units + threads - 1) / threads);
 }
@@ -211,6 +246,16 @@ int launch_dequant(const uint8_t* codes, const float* params, const void* slots,
 int launch_prepare_splits(const int32_t* splits, int32_t* quant, int32_t* merge, int64_t n, cudaStream_t s) {
   if (n == 0) return ROLAQ_OK;
   prepare_splits_kernel<<<blocks_for(n, 256), 256, 0, s>>>(splits, quant, merge, n);
+  return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;
+}
+
+int launch_page_table(const int32_t* req_to_token, int64_t rt_stride, const void* req_idx, int req64,
+                      const void* seq_lens, int seq64, int64_t batch, int32_t max_pages, int32_t* page_table,
+                      int64_t pt_stride, int32_t* seq_out, int32_t* err, cudaStream_t s) {
+  if (batch == 0 || max_pages == 0) return ROLAQ_OK;
+  const dim3 grid(static_cast<unsigned>((max_pages + 7) / 8), static_cast<unsigned>(batch));
+  page_table_kernel<<<grid, 256, 0, s>>>(req_to_token, rt_stride, req_idx, req64, seq_lens, seq64, batch, max_pages,
+                                         page_table, pt_stride, seq_out, err);
   return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;
 }
 

@@ -86,6 +86,10 @@ int launch_dequant(const uint8_t* codes, const float* params, const void* slots,
                    cudaStream_t s);
 int launch_prepare_splits(const int32_t* splits, int32_t* quant, int32_t* merge, int64_t n, cudaStream_t s);
 
+int launch_page_table(const int32_t* req_to_token, int64_t rt_stride, const void* req_idx, int req64,
+                      const void* seq_lens, int seq64, int64_t batch, int32_t max_pages, int32_t* page_table,
+                      int64_t pt_stride, int32_t* seq_out, int32_t* err, cudaStream_t s);
+
 // proj.cu
 int launch_proj(const ProjArgs& a, cudaStream_t s);
 

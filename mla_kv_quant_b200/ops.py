@@ -350,3 +350,25 @@ def project_output(o: torch.Tensor, w_vc: torch.Tensor, out: torch.Tensor, err: 
         raise ValueError("out must be [B, H, Dv]; rows contiguous")
     _lib.call("rolaq_project_output", o.data_ptr(), o.stride(0), o.stride(1), w_vc.data_ptr(), b, h, d, dv,
               out.data_ptr(), out.stride(0), out.stride(1), _err_ptr(err), _lib.stream_ptr())
+
+
+def page_table_from_req_to_token(req_to_token: torch.Tensor, req_pool_indices: torch.Tensor, seq_lens: torch.Tensor,
+                                 page_table: torch.Tensor, seq_lens_out: torch.Tensor | None = None,
+                                 err: torch.Tensor | None = None) -> None:
+    """``rolaq_page_table_from_req_to_token``: the reader's 64-token page table (and int32
+    lengths) from SGLang's ``req_to_token`` map, one launch, no host sync."""
+    _check(req_to_token, "req_to_token", torch.int32, 2)
+    _check(page_table, "page_table", torch.int32, 2)
+    if req_to_token.stride(1) != 1 or page_table.stride(1) != 1:
+        raise ValueError("req_to_token / page_table rows must be contiguous")
+    rp, r64 = _index(req_pool_indices, "req_pool_indices")
+    sp, s64 = _index(seq_lens, "seq_lens")
+    b = req_pool_indices.numel()
+    if seq_lens.numel() < b or page_table.shape[0] < b:
+        raise ValueError("seq_lens / page_table have fewer rows than req_pool_indices")
+    max_pages = min(page_table.shape[1], req_to_token.shape[1] // PAGE)
+    if seq_lens_out is not None and (seq_lens_out.dtype != torch.int32 or seq_lens_out.numel() < b):
+        raise ValueError("seq_lens_out must be int32 with one entry per request")
+    _lib.call("rolaq_page_table_from_req_to_token", req_to_token.data_ptr(), req_to_token.stride(0), rp, r64, sp,
+              s64, b, max_pages, page_table.data_ptr(), page_table.stride(0), _lib.ptr(seq_lens_out), _err_ptr(err),
+              _lib.stream_ptr())

@@ -2,9 +2,8 @@
 
 Each rank owns one contiguous, page-aligned slice of every request's positions
 (and the cache pages of that slice).  It runs the packed decode kernel restricted
-to its slice (``token_range``), which merges its own splits into one partial
-``(o, lse)`` per (request, head) (``o`` rounded to BF16 once, like the final output),
-and the ranks exchange those partials with one NCCL ``all_gather_into_tensor`` of
+to its slice (``token_range``) and merges its own splits into one FP32 partial
+``(o, lse)`` per (request, head); the ranks exchange those partials with one NCCL ``all_gather_into_tensor`` of
 ``B * H * (D + 4) * 4`` bytes per rank, about 33 KB for one DeepSeek-V2-Lite request.  Every rank then merges the ``world`` partials
 with the same LSE kernel and holds the full output.
 
@@ -71,18 +70,22 @@ class SequenceSplitDecoder:
         self.rank = dist.get_rank(group)
 
     def local_partial(self, q, layer_id, page_table, seq_lens, sm_scale, num_splits, token_range):
-        """This rank's slice: the decode call's merged output (BF16) and its LSE, per
-        (request, head).  The output is rounded to BF16 once here, as the final output is."""
+        """This rank's slice: its split partials LSE-merged in FP32, ``(o [B*H, D], lse [B*H])``.
+        The partial stays FP32 through the exchange, so the final output is rounded to BF16
+        once, after the cross-rank merge."""
         b, h, _ = q.shape
         d = self.pool.kv_lora_rank
         parts = num_splits + 1
         part_o = torch.empty(b, h, parts, d, dtype=torch.float32, device=q.device)
         part_lse = torch.empty(b, h, parts, dtype=torch.float32, device=q.device)
-        o = torch.empty(b, h, d, dtype=torch.bfloat16, device=q.device)
-        lse = torch.empty(b, h, dtype=torch.float32, device=q.device)
+        scratch = torch.empty(b, h, d, dtype=torch.bfloat16, device=q.device)
         ops.packed_decode(q, self.pool.layer_view(layer_id), page_table, seq_lens, sm_scale, num_splits, part_o,
-                          part_lse, o, out_lse=lse, token_range=token_range)
-        return o.view(b * h, d), lse.view(b * h)
+                          part_lse, scratch, token_range=token_range)
+        o = torch.empty(b * h, d, dtype=torch.float32, device=q.device)
+        lse = torch.empty(b * h, dtype=torch.float32, device=q.device)
+        ops.merge_partials(part_o.view(b * h, parts, d).transpose(0, 1), part_lse.view(b * h, parts).t(), out_f32=o,
+                           out_lse=lse)
+        return o, lse
 
     def decode(self, q, layer_id, page_table, seq_lens_host: list[int], seq_lens, sm_scale, num_splits=4):
         """``q [B, H, D + Dr]`` -> ``out [B, H, D]`` BF16 on every rank."""

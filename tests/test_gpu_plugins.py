@@ -210,3 +210,89 @@ def test_decode_write_unrotated_and_uniform(monkeypatch, lloyd_max):
         assert np.array_equal(pool.c_codes[li].cpu().numpy()[s], ocodec.pack(oc))
         assert np.array_equal(pool.c_params[li].cpu().numpy()[s], prm)
         assert np.array_equal(bits(pool.rope_buf[li])[s], bits(pe))
+
+
+def test_backend_shim_from_req_to_token():
+    """The decode-backend shim builds the page table from SGLang's token map and decodes
+    exactly what the reader gives with the explicit page table; a page whose tokens are not
+    one aligned run of 64 slots is reported and skipped."""
+    from mla_kv_quant_b200.backend import PackedMLADecodeBackend
+
+    d, dr, h = 512, 64, 16
+    lens = [300, 64, 1, 777]
+    b = len(lens)
+    pool = PackedLatentPool(64 * 40, 1, max_reqs=8, rotations={0: synth.rotation(d, 3)})
+    g = torch.Generator().manual_seed(4)
+    pages = (torch.randperm(39, generator=g) + 1).to(torch.int32)
+    mp = 13
+    pt = pages[: b * mp].reshape(b, mp).cuda()
+    req_idx = torch.tensor([5, 0, 7, 2], device="cuda")  # pool rows of the requests
+    req_to_token = torch.zeros(8, 64 * 16, dtype=torch.int32, device="cuda")
+    for i, L in enumerate(lens):
+        pos = torch.arange(L, device="cuda")
+        slots = pt[i, pos // 64] * 64 + pos % 64
+        req_to_token[req_idx[i], :L] = slots.int()
+        x = synth.latents(L, d, seed=i, device="cuda")
+        pe = synth.normal_bf16((L, dr), seed=10 + i, device="cuda")
+        pool.set_window_meta(False, torch.full((L,), L, dtype=torch.int32, device="cuda"),
+                             torch.full((L,), int(req_idx[i]), dtype=torch.int64, device="cuda"))
+        pool.set_kv_buffer(0, slots.long(), x, pe, positions=pos.int())
+    seq = torch.tensor(lens, dtype=torch.int64, device="cuda")
+    be = PackedMLADecodeBackend(pool, h, max_batch=8, max_context_len=64 * 16, sm_scale=0.07, num_kv_splits=3)
+    be.init_forward_metadata(req_to_token, req_idx, seq)
+    q = synth.normal_bf16((b, h, d + dr), seed=9, device="cuda")
+    got = be.forward_decode(q.view(b, -1), 0)
+    ref = packed_mla_decode_gf_fwd(q, pool, 0, pt, seq.int(), 0.07, 3)
+    torch.cuda.synchronize()
+    assert int(be.err.item()) == 0
+    for i, L in enumerate(lens):
+        n = (L + 63) // 64
+        assert torch.equal(be.page_table[i, :n].cpu(), pt[i, :n].cpu())
+        assert bool((be.page_table[i, n:] == -1).all())
+    assert torch.equal(got, ref)
+    # a request whose second page is not one aligned run of slots
+    req_to_token[req_idx[0], 64 + 5] += 1
+    be.init_forward_metadata(req_to_token, req_idx, seq)
+    torch.cuda.synchronize()
+    assert int(be.err.item()) & 2  # DEV_BAD_PAGE
+    assert int(be.page_table[0, 1].item()) == -1 and int(be.page_table[0, 0].item()) == int(pt[0, 0].item())
+
+
+def test_hf_window_lifecycle_on_gpu(golden_dir):
+    """The HF path's s4r16 window on the GPU: a 30-token prefill and 25 decode steps (batch 2,
+    the second row left-padded by 3, the pad mask growing with the sequence as HF passes it).
+    The row states and the number of rows re-quantized on leaving the window follow the
+    oracle's window rules step by step; window rows are their BF16 input bit for bit; every
+    quantized row equals the CPU oracle's rotate_quantize of its own input (quantized once,
+    never twice), up to rounding ties of the FP32 rotation."""
+    from mla_kv_quant_b200.hf_window import WindowedLatentCache
+    from oracle import quantizer as oquant
+    from oracle import window as owindow
+
+    q = LearnedRotationQuantizer(golden_dir / "artifact_d256")
+    d, b, pre, steps, pad = 256, 2, 30, 25, 3
+    total = pre + steps
+    pad_mask = np.ones((b, total), bool)
+    pad_mask[1, :pad] = False
+    cache = WindowedLatentCache(q, 4, 16)
+    x = synth.latents(b * total, d, seed=3, device="cuda").view(b, 1, total, d)
+    expect_state, expect_moves = None, 0
+    for lo, hi in [(0, pre)] + [(t, t + 1) for t in range(pre, total)]:
+        cache.pad_mask = torch.from_numpy(pad_mask[:, :hi]).cuda()
+        keys = cache.update(x[:, :, lo:hi], 1)
+        tgt = owindow.target_state(pad_mask[:, :hi], 4, 16)
+        if expect_state is not None:
+            tgt[:, :lo] = np.maximum(tgt[:, :lo], expect_state)
+            expect_moves += int(((expect_state == 1) & (tgt[:, :lo] == 2)).sum())
+        expect_state = tgt
+        assert np.array_equal(cache.row_state[1].cpu().numpy(), expect_state)
+    torch.cuda.synchronize()
+    assert cache.stats["requantized_rows"] == expect_moves > 0
+    keys, xin = keys.cpu(), x.cpu()
+    window = torch.from_numpy(expect_state == 1)
+    quant = torch.from_numpy(expect_state == 2)
+    assert torch.equal(keys[:, 0][window], xin[:, 0][window])
+    rows = xin[:, 0][quant].float().numpy()
+    ref = oquant.rotate_quantize(rows, q.rotations[1].numpy(), q.params[1][0], q.params[1][1])
+    got = keys[:, 0][quant].float().numpy()
+    assert np.mean(got == ref) > 0.99 and np.max(np.abs(got - ref)) < 0.05 * np.abs(ref).max()
