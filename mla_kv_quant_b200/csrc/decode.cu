@@ -1169,7 +1169,9 @@ static int launch_window_t(const DecodeArgs& a, cudaStream_t s) {
 }
 
 bool decode_tc_supported(const DecodeArgs& a, int heads);
-int launch_decode_tc(const DecodeArgs& a, int heads, cudaStream_t s);
+int launch_decode_tc(const DecodeArgs& a, int heads, cudaStream_t s, bool dependent = false);
+int launch_decode_windowed(const DecodeArgs& a, int heads, uint16_t* out, int64_t out_sb, int64_t out_sh,
+                           float* out_lse, cudaStream_t s);
 
 int launch_decode(const DecodeArgs& a, int heads, cudaStream_t s) {
   const int d = a.cache.latent_dim, dr = a.cache.rope_dim;
@@ -1214,11 +1216,20 @@ int launch_merge(const float* part_o, int64_t row_stride, int64_t part_stride, c
 // ROLAQ_EUNSUPPORTED and the caller runs launch_decode + launch_merge.
 int launch_decode_merged(const DecodeArgs& a, int heads, uint16_t* out, int64_t out_sb, int64_t out_sh,
                          float* out_lse, cudaStream_t s) {
-  if (!decode_tc_supported(a, heads) || a.cache.latent_dim != 512) return ROLAQ_EUNSUPPORTED;
+  if (!decode_tc_supported(a, heads)) return ROLAQ_EUNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(out) & 7u) || (out_sb & 3) || (out_sh & 3) ||
       (reinterpret_cast<uintptr_t>(a.part_o) & 15u))
     return ROLAQ_EUNSUPPORTED;
   if (heads % kMwHeads != 0) return ROLAQ_EUNSUPPORTED;
+  if (a.cache.latent_dim != 512) {
+    // D = 256: the window split first, the INT2 kernel and the merge as its programmatic
+    // dependents, when the INT2 grid fits one wave (measured 189 against 211 us per layer for
+    // the three separate launches at MiniCPM3's B128 x 8K); with several waves the INT2
+    // kernel's short CTAs wait on the window kernel (measured slower), so the caller takes
+    // the separate launches.
+    if (int64_t(a.batch) * a.num_splits > sm_count()) return ROLAQ_EUNSUPPORTED;
+    return launch_decode_windowed(a, heads, out, out_sb, out_sh, out_lse, s);
+  }
   // the merge kernel stages the window rows (at most sink + recent <= kMaxWindow) as FP32
   constexpr int kMwRowBytes = (512 + 64) * 4;
   static const bool mw_attr = cudaFuncSetAttribute(merge_window_kernel<512, 64>,

@@ -886,6 +886,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+  // Launched as a programmatic dependent of the window kernel: finish only after that grid
+  // has, so that the merge kernel (waiting on this grid) sees the window partials.  Without
+  // a programmatic launch this returns at once.
+  grid_dependency_wait();
 }
 
 }  // namespace tc
@@ -912,7 +916,7 @@ bool decode_tc_supported(const DecodeArgs& a, int heads) {
 }
 
 template <int D, int DR, int H>
-static int launch_tc_t(const DecodeArgs& a, cudaStream_t s) {
+static int launch_tc_t(const DecodeArgs& a, cudaStream_t s, bool dependent) {
   using C = tc::Cfg<D, DR, H>;
   CUtensorMap mr;
   int rc = map_rope(&mr, a.cache.rope, static_cast<uint64_t>(a.cache.num_slots), DR);
@@ -922,14 +926,30 @@ static int launch_tc_t(const DecodeArgs& a, cudaStream_t s) {
                                                    (int)C::SMEM) == cudaSuccess;
   if (!attr_ok) return ROLAQ_ECUDA;
   dim3 grid(a.num_splits, a.batch);
-  tc::decode_tc_kernel<D, DR, H><<<grid, tc::THREADS, C::SMEM, s>>>(mr, a);
+  if (!dependent) {
+    tc::decode_tc_kernel<D, DR, H><<<grid, tc::THREADS, C::SMEM, s>>>(mr, a);
+    return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;
+  }
+  // a programmatic dependent of the kernel before it in the stream (the window split)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(tc::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, tc::decode_tc_kernel<D, DR, H>, mr, a) != cudaSuccess) return ROLAQ_ECUDA;
   return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;
 }
 
-int launch_decode_tc(const DecodeArgs& a, int heads, cudaStream_t s) {
+int launch_decode_tc(const DecodeArgs& a, int heads, cudaStream_t s, bool dependent) {
   const int d = a.cache.latent_dim;
-  if (d == 512) return heads == 16 ? launch_tc_t<512, 64, 16>(a, s) : launch_tc_t<512, 64, 8>(a, s);
-  return heads == 40 ? launch_tc_t<256, 32, 40>(a, s) : launch_tc_t<256, 32, 16>(a, s);
+  if (d == 512)
+    return heads == 16 ? launch_tc_t<512, 64, 16>(a, s, dependent) : launch_tc_t<512, 64, 8>(a, s, dependent);
+  return heads == 40 ? launch_tc_t<256, 32, 40>(a, s, dependent) : launch_tc_t<256, 32, 16>(a, s, dependent);
 }
 
 }  // namespace rolaq

@@ -1,0 +1,317 @@
+// The window split and the final merge of the packed decode, as the two kernels around the
+// tcgen05 INT2 kernel:
+//
+//   window_split_kernel  ->  decode_tc_kernel (programmatic dependent)  ->  merge_splits_kernel
+//                                                                          (programmatic dependent)
+//
+// Reference behaviour: upstream _fwd_hp_window_stage1 and stage 2 of packed_mla_decode_gf_fwd
+// (called at deployment/patches/rolaq_sglang.patch:98-111): the sink/recent tokens are
+// attended from their BF16 ring rows (hp_c, owned by the slot) or, when the ring row has been
+// taken over, from the INT2 codes; that window split and the INT2 splits are merged by
+// log-sum-exp.
+//
+// The window split is a few dependent memory round trips per request (page -> slot -> ring
+// row -> row), so it is given few SMs: one CTA serves `rpc` requests (all heads) and stages
+// their window rows once in shared memory as FP32.  It lets the INT2 kernel launch at once
+// (griddepcontrol.launch_dependents), so the INT2 CTAs fill every other SM while it runs.
+// The merge kernel is launched as a dependent of the INT2 kernel: its CTAs are placed as the
+// INT2 grid's last CTAs retire and wait (griddepcontrol.wait) for that grid, which itself
+// waits for the window kernel before it exits.
+#include "kernels.cuh"
+
+namespace rolaq {
+namespace win {
+
+constexpr int kMaxWindow = 32;  // sink + recent (checked by the host)
+constexpr int THREADS = 1024;
+constexpr int kPage = 64;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  return v;
+}
+
+// Window positions of request b: [s1, e1) u [s2, e2) (sink part, recent part), restricted
+// to the request's token range; returns the row count.
+__device__ __forceinline__ int window_rows(const DecodeArgs& a, int b, int& s1, int& n1, int& s2) {
+  int L = a.seq_lens[b];
+  if (L < 0) L = 0;
+  if (L > a.max_pages * kPage) L = a.max_pages * kPage;
+  const int P = a.cache.sink, W = a.cache.recent;
+  const int lo = min(P, L);
+  const int hs = max(lo, L - W);
+  int rs = 0, re = L;
+  if (a.token_range != nullptr) {
+    rs = max(0, a.token_range[2 * b]);
+    re = min(L, a.token_range[2 * b + 1]);
+  }
+  s1 = min(max(rs, 0), lo);
+  const int e1 = max(min(re, lo), s1);
+  s2 = min(max(rs, hs), L);
+  const int e2 = max(min(re, L), s2);
+  n1 = e1 - s1;
+  return n1 + (e2 - s2);
+}
+
+// One CTA per `rpc` requests.  Dynamic shared memory: FP32 rows [rpc][nwmax][D + DR], then
+// slot and ring-row indices [rpc][kMaxWindow] (int64) and the row counts [rpc].
+template <int D, int DR, int H>
+__global__ void __launch_bounds__(THREADS, 1) window_split_kernel(const DecodeArgs a, int rpc) {
+  constexpr int KW = D + DR;
+  constexpr int EL = D / 32, RL = DR / 32;  // latent / rope elements per lane
+  static_assert(EL % 4 == 0 && RL >= 1, "lane slices");
+  extern __shared__ float4 smem4[];
+  const int nwmax = a.cache.sink + a.cache.recent;
+  float* rows = reinterpret_cast<float*>(smem4);
+  int64_t* rslot = reinterpret_cast<int64_t*>(rows + size_t(rpc) * nwmax * KW);
+  int64_t* rrow = rslot + rpc * kMaxWindow;
+  int* nwv = reinterpret_cast<int*>(rrow + rpc * kMaxWindow);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) grid_launch_dependents();  // the INT2 kernel may start on the other SMs now
+  const int b0 = blockIdx.x * rpc;
+  const int S = a.num_splits + 1;
+
+  // -- per (request, row): slot and the ring row that holds it (if it still belongs to it) --
+  for (int idx = tid; idx < rpc * kMaxWindow; idx += THREADS) {
+    const int r = idx / kMaxWindow, p = idx % kMaxWindow, b = b0 + r;
+    int64_t slot = -1, rr = -1;
+    if (b < a.batch) {
+      int s1, n1, s2;
+      const int nw = window_rows(a, b, s1, n1, s2);
+      if (p == 0) nwv[r] = nw;
+      if (p < nw) {
+        const int pos = p < n1 ? s1 + p : s2 + (p - n1);
+        const int64_t page = a.page_table[b * a.pt_stride + pos / kPage];
+        if (page >= 0 && (page + 1) * kPage <= a.cache.num_slots) {
+          slot = page * kPage + pos % kPage;
+          rr = a.cache.rows ? a.cache.rows[slot] : -1;
+          if (!(rr >= 0 && rr < a.cache.num_ring_rows && a.cache.owners[rr] == slot)) rr = -1;
+        } else {
+          report(a.err, ROLAQ_DEV_BAD_PAGE);
+        }
+      }
+    } else if (p == 0) {
+      nwv[r] = 0;
+    }
+    rslot[idx] = slot;
+    rrow[idx] = rr;
+  }
+  __syncthreads();
+  // -- the rows into shared memory as FP32, four values per thread and step: latent values
+  //    from the BF16 ring row or (ring row taken over) (code - zero) * scale, rope values
+  //    from k_pe; absent rows stay zero --
+  constexpr int C4 = KW / 4;
+  for (int idx = tid; idx < rpc * nwmax * C4; idx += THREADS) {
+    const int r = idx / (nwmax * C4), rem = idx % (nwmax * C4), p = rem / C4, e4 = 4 * (rem % C4);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int64_t slot = rslot[r * kMaxWindow + p], rr = rrow[r * kMaxWindow + p];
+    if (p < nwv[r] && slot >= 0) {
+      if (e4 >= D) {
+        const uint2 w = *reinterpret_cast<const uint2*>(a.cache.rope + slot * DR + (e4 - D));
+        v = make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xFFFF0000u), __uint_as_float(w.y << 16),
+                        __uint_as_float(w.y & 0xFFFF0000u));
+      } else if (rr >= 0) {
+        const uint2 w = *reinterpret_cast<const uint2*>(a.cache.hp + rr * D + e4);
+        v = make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xFFFF0000u), __uint_as_float(w.y << 16),
+                        __uint_as_float(w.y & 0xFFFF0000u));
+      } else {
+        const uint32_t cb = a.cache.codes[slot * (D / 4) + e4 / 4];
+        const float2 sz = reinterpret_cast<const float2*>(a.cache.params)[slot * (D / 128) + e4 / 128];
+        v = make_float4(__fmul_rn(__fsub_rn(static_cast<float>(cb & 3u), sz.y), sz.x),
+                        __fmul_rn(__fsub_rn(static_cast<float>((cb >> 2) & 3u), sz.y), sz.x),
+                        __fmul_rn(__fsub_rn(static_cast<float>((cb >> 4) & 3u), sz.y), sz.x),
+                        __fmul_rn(__fsub_rn(static_cast<float>((cb >> 6) & 3u), sz.y), sz.x));
+      }
+    }
+    reinterpret_cast<float4*>(rows)[(size_t(r) * nwmax + p) * C4 + e4 / 4] = v;
+  }
+  __syncthreads();
+  // -- a warp per (request, head): scores (lane = latent slice), softmax over the rows (lane
+  //    p holds row p), the window partial --
+  for (int pair = warp; pair < rpc * H; pair += THREADS / 32) {
+    const int r = pair / H, h = pair % H, b = b0 + r;
+    if (b >= a.batch) continue;
+    const int nw = nwv[r];
+    const uint16_t* qh = a.q + b * a.q_sb + h * a.q_sh;
+    float qv[EL], qr[RL];
+#pragma unroll
+    for (int c = 0; c < EL / 4; ++c) {
+      const uint2 w = *reinterpret_cast<const uint2*>(qh + EL * lane + 4 * c);
+      qv[4 * c] = __uint_as_float(w.x << 16);
+      qv[4 * c + 1] = __uint_as_float(w.x & 0xFFFF0000u);
+      qv[4 * c + 2] = __uint_as_float(w.y << 16);
+      qv[4 * c + 3] = __uint_as_float(w.y & 0xFFFF0000u);
+    }
+#pragma unroll
+    for (int c = 0; c < RL; ++c) qr[c] = __uint_as_float(static_cast<uint32_t>(qh[D + RL * lane + c]) << 16);
+    const float* rbase = rows + size_t(r) * nwmax * KW;
+    float sp = -INFINITY;  // lane p: the score of row p
+    for (int p = 0; p < nw; ++p) {
+      const float* rw = rbase + size_t(p) * KW;
+      float acc = 0.f;
+#pragma unroll
+      for (int c = 0; c < EL / 4; ++c) {
+        const float4 v = *reinterpret_cast<const float4*>(rw + EL * lane + 4 * c);
+        acc = fmaf(qv[4 * c], v.x, acc);
+        acc = fmaf(qv[4 * c + 1], v.y, acc);
+        acc = fmaf(qv[4 * c + 2], v.z, acc);
+        acc = fmaf(qv[4 * c + 3], v.w, acc);
+      }
+#pragma unroll
+      for (int c = 0; c < RL; ++c) acc = fmaf(qr[c], rw[D + RL * lane + c], acc);
+      acc = warp_sum(acc);
+      // a row whose page is out of range takes no weight (the INT2 splits skip such tokens too)
+      if (lane == p) sp = rslot[r * kMaxWindow + p] >= 0 ? acc * a.sm_scale : -INFINITY;
+    }
+    const float m = warp_max(sp);
+    const float e = sp != -INFINITY ? __expf(sp - m) : 0.f;
+    const float l = warp_sum(e);
+    float o[EL];
+#pragma unroll
+    for (int c = 0; c < EL; ++c) o[c] = 0.f;
+    for (int p = 0; p < nw; ++p) {
+      const float w = __shfl_sync(0xFFFFFFFFu, e, p);
+      const float* rw = rbase + size_t(p) * KW + EL * lane;
+#pragma unroll
+      for (int c = 0; c < EL / 4; ++c) {
+        const float4 v = *reinterpret_cast<const float4*>(rw + 4 * c);
+        o[4 * c] = fmaf(w, v.x, o[4 * c]);
+        o[4 * c + 1] = fmaf(w, v.y, o[4 * c + 1]);
+        o[4 * c + 2] = fmaf(w, v.z, o[4 * c + 2]);
+        o[4 * c + 3] = fmaf(w, v.w, o[4 * c + 3]);
+      }
+    }
+    const float il = l > 0.f ? 1.f / l : 0.f;
+    const int64_t row = (static_cast<int64_t>(b) * H + h) * S + a.num_splits;
+    float4* dst = reinterpret_cast<float4*>(a.part_o + row * D + EL * lane);
+#pragma unroll
+    for (int c = 0; c < EL / 4; ++c)
+      dst[c] = make_float4(o[4 * c] * il, o[4 * c + 1] * il, o[4 * c + 2] * il, o[4 * c + 3] * il);
+    if (lane == 0) a.part_lse[row] = l > 0.f ? m + logf(l) : -INFINITY;
+  }
+}
+
+// The LSE merge of a request's num_splits + 1 partials (INT2 splits, window split last):
+// one CTA per (request, 4 heads), D / 8 threads per head, 8 elements per thread.
+template <int D>
+__global__ void __launch_bounds__(4 * D / 8) merge_splits_kernel(const DecodeArgs a, int heads,
+                                                                uint16_t* __restrict__ out, int64_t out_sb,
+                                                                int64_t out_sh, float* __restrict__ out_lse) {
+  constexpr int TPH = D / 8;  // threads per head (a multiple of 32)
+  const int hgroups = heads / 4;
+  const int b = blockIdx.x / hgroups, h = (blockIdx.x % hgroups) * 4 + threadIdx.x / TPH;
+  const int j = 8 * (threadIdx.x % TPH), lane = threadIdx.x & 31;
+  const int S = a.num_splits + 1;
+  grid_dependency_wait();  // the INT2 kernel (and through it the window kernel) has completed
+  const int64_t row = static_cast<int64_t>(b) * heads + h;
+  const float* lse_row = a.part_lse + row * S;
+  const float* prow = a.part_o + row * S * D + j;
+  float m = -INFINITY;
+  for (int p = lane; p < S; p += 32) m = fmaxf(m, lse_row[p]);
+  m = warp_max(m);
+  const float mref = m == -INFINITY ? 0.f : m;
+  float acc[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) acc[c] = 0.f;
+  float den = 0.f;
+  for (int pb = 0; pb < S; pb += 32) {
+    const int cnt = min(32, S - pb);
+    const float lv = lane < cnt ? lse_row[pb + lane] : -INFINITY;
+    const float wl = lv != -INFINITY ? __expf(lv - mref) : 0.f;  // weight of split pb + lane
+    den += wl;
+    for (int q = 0; q < cnt; q += 4) {  // four splits' loads in flight at once
+      float4 v[4][2];
+      float w[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        w[u] = __shfl_sync(0xFFFFFFFFu, wl, (q + u) & 31);
+        if (q + u >= cnt) w[u] = 0.f;
+        const float4* src = reinterpret_cast<const float4*>(prow + static_cast<int64_t>(pb + min(q + u, cnt - 1)) * D);
+        v[u][0] = src[0];
+        v[u][1] = src[1];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {  // empty splits (weight 0) are masked, not multiplied
+        const float vv[8] = {v[u][0].x, v[u][0].y, v[u][0].z, v[u][0].w, v[u][1].x, v[u][1].y, v[u][1].z, v[u][1].w};
+#pragma unroll
+        for (int c = 0; c < 8; ++c) acc[c] = w[u] > 0.f ? fmaf(w[u], vv[c], acc[c]) : acc[c];
+      }
+    }
+  }
+  den = warp_sum(den);
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  uint32_t pk[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const __nv_bfloat162 v2 = __floats2bfloat162_rn(acc[2 * c] * inv, acc[2 * c + 1] * inv);
+    pk[c] = *reinterpret_cast<const uint32_t*>(&v2);
+  }
+  uint16_t* orow = out + b * out_sb + h * out_sh + j;
+  reinterpret_cast<uint2*>(orow)[0] = make_uint2(pk[0], pk[1]);
+  reinterpret_cast<uint2*>(orow)[1] = make_uint2(pk[2], pk[3]);
+  if (threadIdx.x % TPH == 0 && out_lse) out_lse[row] = den > 0.f ? mref + logf(den) : -INFINITY;
+}
+
+}  // namespace win
+
+// Window split (normal launch), then the INT2 kernel and the merge as programmatic
+// dependents.  Shapes and output alignment are checked by the caller.
+int launch_decode_tc(const DecodeArgs& a, int heads, cudaStream_t s, bool dependent);
+
+template <int D, int DR, int H>
+static int launch_window_split(const DecodeArgs& a, cudaStream_t s) {
+  const int nwmax = a.cache.sink + a.cache.recent;
+  const size_t per_req = size_t(nwmax) * (D + DR) * 4 + 2 * win::kMaxWindow * 8 + 4;
+  const size_t budget = 200 * 1024;
+  int rpc = nwmax > 0 ? static_cast<int>(budget / per_req) : 64;
+  rpc = max(1, min(rpc, 8));
+  const size_t smem = size_t(rpc) * per_req + 16;
+  static const bool attr = cudaFuncSetAttribute(win::window_split_kernel<D, DR, H>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                (int)(208 * 1024)) == cudaSuccess;
+  if (!attr) return ROLAQ_ECUDA;
+  win::window_split_kernel<D, DR, H><<<static_cast<unsigned>((a.batch + rpc - 1) / rpc), win::THREADS, smem, s>>>(
+      a, rpc);
+  return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;
+}
+
+template <int D>
+static int launch_merge_splits(const DecodeArgs& a, int heads, uint16_t* out, int64_t out_sb, int64_t out_sh,
+                               float* out_lse, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(int64_t(a.batch) * heads / 4));
+  cfg.blockDim = dim3(4 * D / 8);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, win::merge_splits_kernel<D>, a, heads, out, out_sb, out_sh, out_lse) != cudaSuccess)
+    return ROLAQ_ECUDA;
+  return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;
+}
+
+int launch_decode_windowed(const DecodeArgs& a, int heads, uint16_t* out, int64_t out_sb, int64_t out_sh,
+                           float* out_lse, cudaStream_t s) {
+  const int d = a.cache.latent_dim;
+  int rc;
+  if (d == 512)
+    rc = heads == 16 ? launch_window_split<512, 64, 16>(a, s) : launch_window_split<512, 64, 8>(a, s);
+  else
+    rc = heads == 40 ? launch_window_split<256, 32, 40>(a, s) : launch_window_split<256, 32, 16>(a, s);
+  if (rc != ROLAQ_OK) return rc;
+  rc = launch_decode_tc(a, heads, s, true);
+  if (rc != ROLAQ_OK) return rc;
+  return d == 512 ? launch_merge_splits<512>(a, heads, out, out_sb, out_sh, out_lse, s)
+                  : launch_merge_splits<256>(a, heads, out, out_sb, out_sh, out_lse, s);
+}
+
+}  // namespace rolaq

@@ -290,22 +290,22 @@ def merge_partials(part_o: torch.Tensor, part_lse: torch.Tensor, out_bf16: torch
 
 def default_num_splits(batch: int, max_ctx: int, sm_count: int = 148, ctas_per_sm: int | None = None,
                        latent_dim: int = 512, rope_dim: int = 64, heads: int = 16) -> int:
-    """Pick the number of INT2 KV splits per request so that ``batch * splits`` CTAs
-    fill whole waves of the GPU and each split keeps at least 4 pages.  The tcgen05
-    kernel (every built shape) holds one CTA per SM."""
+    """Pick the number of INT2 KV splits per request: the count that minimises
+    ``waves * (tiles per split + 3)``, where a wave is ``sm_count * ctas_per_sm`` CTAs, a tile is
+    128 tokens and the 3 is a CTA's fixed cost (set-up, query conversion, epilogue) in tiles,
+    fitted to split-count sweeps on B200 (B64 x 16K: 9 splits; B128 x 8K: 2-3).  Ties go to
+    fewer splits.  The tcgen05 kernel (every built shape) holds one CTA per SM."""
     if ctas_per_sm is None:
         tc = {(512, 64, 16), (512, 64, 8), (256, 32, 40), (256, 32, 16)}
         ctas_per_sm = 1 if (latent_dim, rope_dim, heads) in tc else 2
-    pages = max(1, math.ceil(max_ctx / PAGE))
+    tiles = max(1, math.ceil(max_ctx / (2 * PAGE)))
     slots = sm_count * ctas_per_sm
     best, best_cost = 1, float("inf")
-    for s in range(1, min(pages, 128) + 1):
-        ctas = batch * s
-        waves = math.ceil(ctas / slots)
-        pps = math.ceil(pages / s)
-        cost = waves * (pps + 2)  # per-split fixed cost ~ 2 pages of work
-        if pps < 4 and s > 1:
+    for s in range(1, min(tiles, 128) + 1):
+        tps = math.ceil(tiles / s)
+        if tps < 2 and s > 1:
             break
+        cost = math.ceil(batch * s / slots) * (tps + 3)
         if cost < best_cost:
             best, best_cost = s, cost
     return best

@@ -8,7 +8,7 @@
   of the codes differ (rounding ties); k_pe, ring rows and maps equal the oracle
   writer's.
 * Decode, config 2: 64 requests x 16384 tokens with the benchmark's default split
-  count (9), through the caller-scratch and the static-scratch entry points, a seeded
+  count and with 9 splits (15 / 14 tiles per CTA), through the caller-scratch and the static-scratch entry points, a seeded
   subset of 8 requests against the FP64 oracle with the decode tests' tolerance: the
   kernel's FP32 result (its partials merged in FP32) within max-abs 2e-2, the BF16 output
   within 2e-2 plus half a BF16 ulp of the value (the output format's own rounding),
@@ -84,7 +84,8 @@ def config2_pool():
     return pool, pt, seq_lens
 
 
-def test_decode_config2_default_splits(config2_pool):
+@pytest.mark.parametrize("which", ["default", "nine"])
+def test_decode_config2_default_splits(config2_pool, which):
     import ctypes
 
     from mla_kv_quant_b200 import _lib
@@ -92,8 +93,8 @@ def test_decode_config2_default_splits(config2_pool):
     pool, pt, seq_lens = config2_pool
     d, dr, h = 512, 64, 16
     b = len(seq_lens)
-    splits = ops.default_num_splits(b, CTX)
-    assert splits == 9
+    # the bench's split count, and 9 (15 / 14 tiles per split: many tiles per CTA)
+    splits = ops.default_num_splits(b, CTX) if which == "default" else 9
     q = synth.normal_bf16((b, h, d + dr), seed=54, device="cuda")
     sl = torch.tensor(seq_lens, dtype=torch.int32, device="cuda")
     out = torch.full((b, h, d), float("nan"), dtype=torch.bfloat16, device="cuda")
@@ -126,7 +127,7 @@ def test_decode_config2_default_splits(config2_pool):
     f = o32.view(b, h, d).cpu().numpy()
     for i in sub:
         e32 = np.abs(f[i] - ref[i]).max()
-        print(f"request {i}: FP32 max-abs {e32:.4g}, max |ref| {np.abs(ref[i]).max():.3g}")
+        print(f"splits {splits} request {i}: FP32 max-abs {e32:.4g}, max |ref| {np.abs(ref[i]).max():.3g}")
         assert e32 <= 2e-2, f"request {i}: FP32 max-abs {e32}"
         half_ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(ref[i]), 1e-30))) - 8)
         assert np.max(np.abs(o[i] - ref[i]) - half_ulp) <= 2e-2, f"request {i}"
@@ -134,10 +135,12 @@ def test_decode_config2_default_splits(config2_pool):
     assert np.allclose(lse.cpu().numpy()[sub], ref_lse[sub], atol=2e-3)
 
 
-def test_decode_minicpm3_shape_default_splits():
+@pytest.mark.parametrize("which", ["default", "many"])
+def test_decode_minicpm3_shape_default_splits(which):
     """The MiniCPM3-4B shape (D = 256, Dr = 32, H = 40, softmax scale 1/sqrt(64 + 32)) on
-    the tcgen05 kernel: 8 requests x 8192 tokens with the default split count, every
-    request against the FP64 oracle."""
+    the tcgen05 kernel: 8 requests x 8192 tokens with the default split count (one wave:
+    the window split runs first) and with 32 splits (two waves: separate window and merge
+    launches), every request against the FP64 oracle."""
     d, dr, h, b, ctx = 256, 32, 40, 8, 8192
     seq_lens = [ctx] * b
     g = torch.Generator().manual_seed(61)
@@ -146,7 +149,7 @@ def test_decode_minicpm3_shape_default_splits():
     pool = GpuPool(64 * (b * pages + 1), d, dr, max_reqs=b, sink=4, recent=16)
     fill_requests(pool, seq_lens, pt, synth.rotation(d, seed=62), ops.codec_serving(0.9, synth.signal_gain(0.9)),
                   seed=63)
-    splits = ops.default_num_splits(b, ctx, latent_dim=d, rope_dim=dr, heads=h)
+    splits = ops.default_num_splits(b, ctx, latent_dim=d, rope_dim=dr, heads=h) if which == "default" else 32
     q = synth.normal_bf16((b, h, d + dr), seed=64, device="cuda")
     sl = torch.tensor(seq_lens, dtype=torch.int32, device="cuda")
     out = torch.empty(b, h, d, dtype=torch.bfloat16, device="cuda")

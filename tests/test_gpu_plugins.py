@@ -221,9 +221,9 @@ def test_backend_shim_from_req_to_token():
     d, dr, h = 512, 64, 16
     lens = [300, 64, 1, 777]
     b = len(lens)
-    pool = PackedLatentPool(64 * 40, 1, max_reqs=8, rotations={0: synth.rotation(d, 3)})
+    pool = PackedLatentPool(64 * 60, 1, max_reqs=8, rotations={0: synth.rotation(d, 3)})
     g = torch.Generator().manual_seed(4)
-    pages = (torch.randperm(39, generator=g) + 1).to(torch.int32)
+    pages = (torch.randperm(59, generator=g) + 1).to(torch.int32)
     mp = 13
     pt = pages[: b * mp].reshape(b, mp).cuda()
     req_idx = torch.tensor([5, 0, 7, 2], device="cuda")  # pool rows of the requests
