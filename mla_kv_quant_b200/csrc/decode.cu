@@ -1221,15 +1221,14 @@ int launch_decode_merged(const DecodeArgs& a, int heads, uint16_t* out, int64_t 
       (reinterpret_cast<uintptr_t>(a.part_o) & 15u))
     return ROLAQ_EUNSUPPORTED;
   if (heads % kMwHeads != 0) return ROLAQ_EUNSUPPORTED;
-  if (a.cache.latent_dim != 512) {
-    // D = 256: the window split first, the INT2 kernel and the merge as its programmatic
-    // dependents, when the INT2 grid fits one wave (measured 189 against 211 us per layer for
-    // the three separate launches at MiniCPM3's B128 x 8K); with several waves the INT2
-    // kernel's short CTAs wait on the window kernel (measured slower), so the caller takes
-    // the separate launches.
-    if (int64_t(a.batch) * a.num_splits > sm_count()) return ROLAQ_EUNSUPPORTED;
+  // When the INT2 grid fits one wave: the window split first, on the SMs the grid leaves
+  // free, and the INT2 kernel and the merge as programmatic dependents.  With several waves
+  // the window CTAs would hold SMs the INT2 grid needs: for D = 512 the window split and the
+  // merge then run in one dependent kernel after the INT2 kernel (below); for D = 256 the
+  // caller takes the separate launches.
+  if (int64_t(a.batch) * a.num_splits < sm_count())
     return launch_decode_windowed(a, heads, out, out_sb, out_sh, out_lse, s);
-  }
+  if (a.cache.latent_dim != 512) return ROLAQ_EUNSUPPORTED;
   // the merge kernel stages the window rows (at most sink + recent <= kMaxWindow) as FP32
   constexpr int kMwRowBytes = (512 + 64) * 4;
   static const bool mw_attr = cudaFuncSetAttribute(merge_window_kernel<512, 64>,

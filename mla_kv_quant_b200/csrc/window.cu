@@ -11,8 +11,9 @@
 // log-sum-exp.
 //
 // The window split is a few dependent memory round trips per request (page -> slot -> ring
-// row -> row), so it is given few SMs: one CTA serves `rpc` requests (all heads) and stages
-// their window rows once in shared memory as FP32.  It lets the INT2 kernel launch at once
+// row -> row), so it is given only the SMs the INT2 grid leaves free (used when that grid fits
+// one wave): a CTA serves several requests (all heads), staging their window rows in shared
+// memory as FP32, a chunk of requests at a time.  It lets the INT2 kernel launch at once
 // (griddepcontrol.launch_dependents), so the INT2 CTAs fill every other SM while it runs.
 // The merge kernel is launched as a dependent of the INT2 kernel: its CTAs are placed as the
 // INT2 grid's last CTAs retire and wait (griddepcontrol.wait) for that grid, which itself
@@ -59,10 +60,13 @@ __device__ __forceinline__ int window_rows(const DecodeArgs& a, int b, int& s1, 
   return n1 + (e2 - s2);
 }
 
-// One CTA per `rpc` requests.  Dynamic shared memory: FP32 rows [rpc][nwmax][D + DR], then
-// slot and ring-row indices [rpc][kMaxWindow] (int64) and the row counts [rpc].
+// A CTA serves `per_cta` requests, `rpc` at a time.  Dynamic shared memory: FP32 rows
+// [rpc][nwmax][D + DR], then slot and ring-row indices [rpc][kMaxWindow] (int64) and the row
+// counts [rpc].
+constexpr int kStageLoads = 12;  // staged 16-byte row pieces per thread and chunk (host-checked)
+
 template <int D, int DR, int H>
-__global__ void __launch_bounds__(THREADS, 1) window_split_kernel(const DecodeArgs a, int rpc) {
+__global__ void __launch_bounds__(THREADS, 1) window_split_kernel(const DecodeArgs a, int rpc, int per_cta) {
   constexpr int KW = D + DR;
   constexpr int EL = D / 32, RL = DR / 32;  // latent / rope elements per lane
   static_assert(EL % 4 == 0 && RL >= 1, "lane slices");
@@ -74,14 +78,17 @@ __global__ void __launch_bounds__(THREADS, 1) window_split_kernel(const DecodeAr
   int* nwv = reinterpret_cast<int*>(rrow + rpc * kMaxWindow);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) grid_launch_dependents();  // the INT2 kernel may start on the other SMs now
-  const int b0 = blockIdx.x * rpc;
   const int S = a.num_splits + 1;
+  const int bend = min(a.batch, (blockIdx.x + 1) * per_cta);
+  // the CTA's requests, rpc at a time
+  for (int b0 = blockIdx.x * per_cta; b0 < bend; b0 += rpc) {
+  if (b0 > blockIdx.x * per_cta) __syncthreads();  // the previous chunk's rows are no longer read
 
   // -- per (request, row): slot and the ring row that holds it (if it still belongs to it) --
   for (int idx = tid; idx < rpc * kMaxWindow; idx += THREADS) {
     const int r = idx / kMaxWindow, p = idx % kMaxWindow, b = b0 + r;
     int64_t slot = -1, rr = -1;
-    if (b < a.batch) {
+    if (b < bend) {
       int s1, n1, s2;
       const int nw = window_rows(a, b, s1, n1, s2);
       if (p == 0) nwv[r] = nw;
@@ -107,36 +114,53 @@ __global__ void __launch_bounds__(THREADS, 1) window_split_kernel(const DecodeAr
   //    from the BF16 ring row or (ring row taken over) (code - zero) * scale, rope values
   //    from k_pe; absent rows stay zero --
   constexpr int C4 = KW / 4;
-  for (int idx = tid; idx < rpc * nwmax * C4; idx += THREADS) {
-    const int r = idx / (nwmax * C4), rem = idx % (nwmax * C4), p = rem / C4, e4 = 4 * (rem % C4);
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    const int64_t slot = rslot[r * kMaxWindow + p], rr = rrow[r * kMaxWindow + p];
-    if (p < nwv[r] && slot >= 0) {
-      if (e4 >= D) {
-        const uint2 w = *reinterpret_cast<const uint2*>(a.cache.rope + slot * DR + (e4 - D));
-        v = make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xFFFF0000u), __uint_as_float(w.y << 16),
-                        __uint_as_float(w.y & 0xFFFF0000u));
-      } else if (rr >= 0) {
-        const uint2 w = *reinterpret_cast<const uint2*>(a.cache.hp + rr * D + e4);
-        v = make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xFFFF0000u), __uint_as_float(w.y << 16),
-                        __uint_as_float(w.y & 0xFFFF0000u));
-      } else {
+  {
+    // every load of the thread is issued before any is used (one round trip per chunk)
+    const int total = rpc * nwmax * C4;
+    uint2 raw[kStageLoads];
+#pragma unroll
+    for (int k = 0; k < kStageLoads; ++k) {
+      const int idx = tid + k * THREADS;
+      raw[k] = make_uint2(0, 0);
+      if (idx < total) {
+        const int r = idx / (nwmax * C4), rem = idx % (nwmax * C4), p = rem / C4, e4 = 4 * (rem % C4);
+        const int64_t slot = rslot[r * kMaxWindow + p], rr = rrow[r * kMaxWindow + p];
+        if (p < nwv[r] && slot >= 0) {
+          if (e4 >= D)
+            raw[k] = *reinterpret_cast<const uint2*>(a.cache.rope + slot * DR + (e4 - D));
+          else if (rr >= 0)
+            raw[k] = *reinterpret_cast<const uint2*>(a.cache.hp + rr * D + e4);
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kStageLoads; ++k) {
+      const int idx = tid + k * THREADS;
+      if (idx >= total) continue;
+      const int r = idx / (nwmax * C4), rem = idx % (nwmax * C4), p = rem / C4, e4 = 4 * (rem % C4);
+      const int64_t slot = rslot[r * kMaxWindow + p], rr = rrow[r * kMaxWindow + p];
+      float4 v;
+      if (p < nwv[r] && slot >= 0 && e4 < D && rr < 0) {  // ring row taken over (rare): the INT2 codes
         const uint32_t cb = a.cache.codes[slot * (D / 4) + e4 / 4];
         const float2 sz = reinterpret_cast<const float2*>(a.cache.params)[slot * (D / 128) + e4 / 128];
         v = make_float4(__fmul_rn(__fsub_rn(static_cast<float>(cb & 3u), sz.y), sz.x),
                         __fmul_rn(__fsub_rn(static_cast<float>((cb >> 2) & 3u), sz.y), sz.x),
                         __fmul_rn(__fsub_rn(static_cast<float>((cb >> 4) & 3u), sz.y), sz.x),
                         __fmul_rn(__fsub_rn(static_cast<float>((cb >> 6) & 3u), sz.y), sz.x));
+      } else {  // BF16 (ring row or k_pe); absent rows stay zero
+        const uint2 w = raw[k];
+        v = make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xFFFF0000u), __uint_as_float(w.y << 16),
+                        __uint_as_float(w.y & 0xFFFF0000u));
       }
+      reinterpret_cast<float4*>(rows)[(size_t(r) * nwmax + p) * C4 + e4 / 4] = v;
     }
-    reinterpret_cast<float4*>(rows)[(size_t(r) * nwmax + p) * C4 + e4 / 4] = v;
   }
   __syncthreads();
   // -- a warp per (request, head): scores (lane = latent slice), softmax over the rows (lane
   //    p holds row p), the window partial --
   for (int pair = warp; pair < rpc * H; pair += THREADS / 32) {
     const int r = pair / H, h = pair % H, b = b0 + r;
-    if (b >= a.batch) continue;
+    if (b >= bend) continue;
     const int nw = nwv[r];
     const uint16_t* qh = a.q + b * a.q_sb + h * a.q_sh;
     float qv[EL], qr[RL];
@@ -195,6 +219,7 @@ __global__ void __launch_bounds__(THREADS, 1) window_split_kernel(const DecodeAr
       dst[c] = make_float4(o[4 * c] * il, o[4 * c + 1] * il, o[4 * c + 2] * il, o[4 * c + 3] * il);
     if (lane == 0) a.part_lse[row] = l > 0.f ? m + logf(l) : -INFINITY;
   }
+  }  // chunk
 }
 
 // The LSE merge of a request's num_splits + 1 partials (INT2 splits, window split last):
@@ -264,20 +289,26 @@ __global__ void __launch_bounds__(4 * D / 8) merge_splits_kernel(const DecodeArg
 // dependents.  Shapes and output alignment are checked by the caller.
 int launch_decode_tc(const DecodeArgs& a, int heads, cudaStream_t s, bool dependent);
 
+// Requests per chunk (rpc): as many as shared memory and the per-thread staging registers
+// allow.  CTAs: only as many as the SMs the INT2 grid leaves free (its CTAs hold a whole SM
+// each), so that no INT2 CTA waits for a window CTA; each CTA then loops over its requests.
 template <int D, int DR, int H>
 static int launch_window_split(const DecodeArgs& a, cudaStream_t s) {
   const int nwmax = a.cache.sink + a.cache.recent;
   const size_t per_req = size_t(nwmax) * (D + DR) * 4 + 2 * win::kMaxWindow * 8 + 4;
   const size_t budget = 200 * 1024;
-  int rpc = nwmax > 0 ? static_cast<int>(budget / per_req) : 64;
+  int rpc = nwmax > 0 ? static_cast<int>(budget / per_req) : 8;
+  if (nwmax > 0) rpc = min(rpc, (win::kStageLoads * win::THREADS) / (nwmax * (D + DR) / 4));
   rpc = max(1, min(rpc, 8));
+  const int free_sms = max(1, sm_count() - a.batch * a.num_splits);
+  const int ctas = max(1, min((a.batch + rpc - 1) / rpc, free_sms));
+  const int per_cta = (a.batch + ctas - 1) / ctas;
   const size_t smem = size_t(rpc) * per_req + 16;
   static const bool attr = cudaFuncSetAttribute(win::window_split_kernel<D, DR, H>,
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 (int)(208 * 1024)) == cudaSuccess;
   if (!attr) return ROLAQ_ECUDA;
-  win::window_split_kernel<D, DR, H><<<static_cast<unsigned>((a.batch + rpc - 1) / rpc), win::THREADS, smem, s>>>(
-      a, rpc);
+  win::window_split_kernel<D, DR, H><<<static_cast<unsigned>(ctas), win::THREADS, smem, s>>>(a, rpc, per_cta);
   return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;
 }
 
