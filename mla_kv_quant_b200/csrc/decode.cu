@@ -1172,6 +1172,7 @@ bool decode_tc_supported(const DecodeArgs& a, int heads);
 int launch_decode_tc(const DecodeArgs& a, int heads, cudaStream_t s, bool dependent = false);
 int launch_decode_windowed(const DecodeArgs& a, int heads, uint16_t* out, int64_t out_sb, int64_t out_sh,
                            float* out_lse, cudaStream_t s);
+bool window_first_fits(const DecodeArgs& a);
 
 int launch_decode(const DecodeArgs& a, int heads, cudaStream_t s) {
   const int d = a.cache.latent_dim, dr = a.cache.rope_dim;
@@ -1221,13 +1222,14 @@ int launch_decode_merged(const DecodeArgs& a, int heads, uint16_t* out, int64_t 
       (reinterpret_cast<uintptr_t>(a.part_o) & 15u))
     return ROLAQ_EUNSUPPORTED;
   if (heads % kMwHeads != 0) return ROLAQ_EUNSUPPORTED;
-  // When the INT2 grid fits one wave: the window split first, on the SMs the grid leaves
-  // free, and the INT2 kernel and the merge as programmatic dependents.  With several waves
+  // When the INT2 grid and the window CTAs fit on the SMs together: the window split first,
+  // on the SMs the grid leaves free, and the INT2 kernel and the merge as programmatic
+  // dependents (B64 x 16K, 2 splits: 157.6 us per layer in the benchmark step, against 167.8
+  // for the window split and merge after the INT2 kernel).  With several waves
   // the window CTAs would hold SMs the INT2 grid needs: for D = 512 the window split and the
   // merge then run in one dependent kernel after the INT2 kernel (below); for D = 256 the
   // caller takes the separate launches.
-  if (int64_t(a.batch) * a.num_splits < sm_count())
-    return launch_decode_windowed(a, heads, out, out_sb, out_sh, out_lse, s);
+  if (window_first_fits(a)) return launch_decode_windowed(a, heads, out, out_sb, out_sh, out_lse, s);
   if (a.cache.latent_dim != 512) return ROLAQ_EUNSUPPORTED;
   // the merge kernel stages the window rows (at most sink + recent <= kMaxWindow) as FP32
   constexpr int kMwRowBytes = (512 + 64) * 4;

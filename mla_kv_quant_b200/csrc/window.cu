@@ -289,17 +289,32 @@ __global__ void __launch_bounds__(4 * D / 8) merge_splits_kernel(const DecodeArg
 // dependents.  Shapes and output alignment are checked by the caller.
 int launch_decode_tc(const DecodeArgs& a, int heads, cudaStream_t s, bool dependent);
 
-// Requests per chunk (rpc): as many as shared memory and the per-thread staging registers
-// allow.  CTAs: only as many as the SMs the INT2 grid leaves free (its CTAs hold a whole SM
-// each), so that no INT2 CTA waits for a window CTA; each CTA then loops over its requests.
+// Requests per window CTA (rpc): as many as shared memory and the per-thread staging
+// registers allow.
+static int window_rpc(int d, int dr, int nwmax) {
+  if (nwmax <= 0) return 8;
+  const size_t per_req = size_t(nwmax) * (d + dr) * 4 + 2 * win::kMaxWindow * 8 + 4;
+  int rpc = static_cast<int>((200 * 1024) / per_req);
+  rpc = min(rpc, (win::kStageLoads * win::THREADS) / (nwmax * (d + dr) / 4));
+  return max(1, min(rpc, 8));
+}
+
+// The window-first launch applies when the INT2 grid and one window CTA per rpc requests fit
+// on the SMs together: no INT2 CTA then waits for a window CTA (measured at B128 x 8K with
+// D = 512, window CTAs looping over two chunks on the 20 free SMs: 226 against 206 us per
+// layer for the window split after the INT2 kernel).
+bool window_first_fits(const DecodeArgs& a) {
+  const int rpc = window_rpc(a.cache.latent_dim, a.cache.rope_dim, a.cache.sink + a.cache.recent);
+  return int64_t(a.batch) * a.num_splits + (a.batch + rpc - 1) / rpc <= sm_count();
+}
+
+// CTAs: only as many as the SMs the INT2 grid leaves free (its CTAs hold a whole SM each),
+// each looping over its requests rpc at a time.
 template <int D, int DR, int H>
 static int launch_window_split(const DecodeArgs& a, cudaStream_t s) {
   const int nwmax = a.cache.sink + a.cache.recent;
   const size_t per_req = size_t(nwmax) * (D + DR) * 4 + 2 * win::kMaxWindow * 8 + 4;
-  const size_t budget = 200 * 1024;
-  int rpc = nwmax > 0 ? static_cast<int>(budget / per_req) : 8;
-  if (nwmax > 0) rpc = min(rpc, (win::kStageLoads * win::THREADS) / (nwmax * (D + DR) / 4));
-  rpc = max(1, min(rpc, 8));
+  const int rpc = window_rpc(D, DR, nwmax);
   const int free_sms = max(1, sm_count() - a.batch * a.num_splits);
   const int ctas = max(1, min((a.batch + rpc - 1) / rpc, free_sms));
   const int per_cta = (a.batch + ctas - 1) / ctas;
