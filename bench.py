@@ -828,27 +828,42 @@ def profile_layer(args, what):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     batch, ctx = args.batch, args.ctx
+    d, dr, heads, sm = (256, 32, 40, 1 / math.sqrt(96.0)) if args.shape == "minicpm3" else \
+        (D, DR, HEADS, 1 / math.sqrt(192.0))
     pt, num_slots = synth.page_table(batch, ctx, seed=4, device=dev)
-    pool = PackedLatentPool(num_slots, 1, D, DR, max_reqs=batch, sink=SINK, recent=RECENT, device=dev,
-                            rotations={0: synth.rotation(D, 1000)}, quantizer_params=[(0.85, synth.signal_gain(0.85))])
-    fill_cache_layers(pool, pt, batch, ctx, dev, seed=0, layers=1)
+    pool = PackedLatentPool(num_slots, 1, d, dr, max_reqs=batch, sink=SINK, recent=RECENT, device=dev,
+                            rotations={0: synth.rotation(d, 1000)}, quantizer_params=[(0.85, synth.signal_gain(0.85))])
+    if d == D:
+        fill_cache_layers(pool, pt, batch, ctx, dev, seed=0, layers=1)
+    else:
+        pos = torch.arange(ctx, device=dev)
+        for b0 in range(0, batch, 8):
+            bs = list(range(b0, min(batch, b0 + 8)))
+            n = len(bs) * ctx
+            slots = torch.cat([pt[b, pos // 64].long() * 64 + pos % 64 for b in bs])
+            ops.fused_write(synth.latents(n, d, b0, dev), synth.normal_bf16((n, dr), b0 + 1, dev), slots,
+                            pool.write_rotation_t(0), pool.codec(0), pool.layer_view(0),
+                            seq_lens=torch.full((n,), ctx, dtype=torch.int32, device=dev),
+                            req_idx=torch.tensor(bs, device=dev).repeat_interleave(ctx),
+                            positions=pos.repeat(len(bs)).to(torch.int32))
+        torch.cuda.synchronize()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     times = []
     if what == "decode":
-        splits = args.splits or ops.default_num_splits(batch, ctx)
-        q = synth.normal_bf16((batch, HEADS, D + DR), 3, dev)
+        splits = args.splits or ops.default_num_splits(batch, ctx, latent_dim=d, rope_dim=dr, heads=heads)
+        q = synth.normal_bf16((batch, heads, d + dr), 3, dev)
         sl = torch.full((batch,), ctx, dtype=torch.int32, device=dev)
-        po = torch.empty(batch, HEADS, splits + 1, D, device=dev)
-        pl = torch.empty(batch, HEADS, splits + 1, device=dev)
-        out = torch.empty(batch, HEADS, D, dtype=torch.bfloat16, device=dev)
+        po = torch.empty(batch, heads, splits + 1, d, device=dev)
+        pl = torch.empty(batch, heads, splits + 1, device=dev)
+        out = torch.empty(batch, heads, d, dtype=torch.bfloat16, device=dev)
         for _ in range(3):
             ev[0].record()
-            ops.packed_decode(q, pool.layer_view(0), pt, sl, 1 / math.sqrt(192.0), splits, po, pl, out)
+            ops.packed_decode(q, pool.layer_view(0), pt, sl, sm, splits, po, pl, out)
             ev[1].record()
             torch.cuda.synchronize()
             times.append(ev[0].elapsed_time(ev[1]) * 1e3)
-        print(json.dumps({"mode": "decode-layer", "us": times, "splits": splits,
-                          "algorithmic_bytes": decode_bytes(batch, ctx)}))
+        print(json.dumps({"mode": "decode-layer", "shape": args.shape, "us": times, "splits": splits,
+                          "algorithmic_bytes": decode_bytes(batch, ctx, heads=heads, d=d, dr=dr)}))
     else:
         n = 8 * ctx
         x = synth.latents(n, D, 5, dev)
@@ -981,6 +996,9 @@ def main():
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--ctx", type=int, default=16384)
     ap.add_argument("--splits", type=int, default=0, help="INT2 KV splits per request (0: auto)")
+    ap.add_argument("--shape", choices=["dsv2", "minicpm3"], default="dsv2",
+                    help="latent / rope / heads of the *-layer modes: DeepSeek-V2-Lite 512/64/16 or "
+                         "MiniCPM3-4B 256/32/40")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra-configs", action="store_true", help="skip the configs 3a / 3b lines")
     args = ap.parse_args()
