@@ -864,6 +864,25 @@ def profile_layer(args, what):
             times.append(ev[0].elapsed_time(ev[1]) * 1e3)
         print(json.dumps({"mode": "decode-layer", "shape": args.shape, "us": times, "splits": splits,
                           "algorithmic_bytes": decode_bytes(batch, ctx, heads=heads, d=d, dr=dr)}))
+    elif what == "absorbed":
+        from mla_kv_quant_b200 import absorbed
+
+        dn = dv = 128 if d == D else 64
+        w = (synth.normal_bf16((heads * (dn + dv), d), 300, dev).float() * 0.05).to(torch.bfloat16)
+        w_kc, w_vc = absorbed.split_absorbed_weights(w, heads, dn, dv)
+        qn = synth.normal_bf16((batch, heads, dn), 21, dev)
+        qp = synth.normal_bf16((batch, heads, dr), 22, dev)
+        q = torch.empty(batch, heads, d + dr, dtype=torch.bfloat16, device=dev)
+        o = synth.normal_bf16((batch, heads, d), 23, dev)
+        y = torch.empty(batch, heads, dv, dtype=torch.bfloat16, device=dev)
+        for _ in range(3):
+            ev[0].record()
+            absorbed.absorb_query(qn, qp, w_kc, out=q)
+            absorbed.project_output(o, w_vc, out=y)
+            ev[1].record()
+            torch.cuda.synchronize()
+            times.append(ev[0].elapsed_time(ev[1]) * 1e3)
+        print(json.dumps({"mode": "absorbed-layer", "shape": args.shape, "us": times}))
     else:
         n = 8 * ctx
         x = synth.latents(n, D, 5, dev)
@@ -985,7 +1004,8 @@ def run_seqsplit(args, rank, world, dev):
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--mode", choices=["step", "decode-layer", "writer-layer", "seqsplit", "batch4a"], default="step",
+    ap.add_argument("--mode", choices=["step", "decode-layer", "writer-layer", "absorbed-layer", "seqsplit", "batch4a"],
+                    default="step",
                     help="step: the benchmark; *-layer: one layer, 3 launches (for ncu captures); "
                          "seqsplit: one 128K-token request split over the ranks (latency per layer); "
                          "batch4a: 512 requests x 32K sharded over the ranks")
