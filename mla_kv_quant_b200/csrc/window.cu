@@ -24,13 +24,21 @@ namespace rolaq {
 namespace win {
 
 constexpr int kMaxWindow = 32;  // sink + recent (checked by the host)
-constexpr int THREADS = 1024;
+constexpr int THREADS = 512;
 constexpr int kPage = 64;
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
   return v;
+}
+// four BF16 (packed in two words) -> FP32
+__device__ __forceinline__ float4 bf16x4(uint2 w) {
+  return make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xFFFF0000u), __uint_as_float(w.y << 16),
+                     __uint_as_float(w.y & 0xFFFF0000u));
+}
+__device__ __forceinline__ float dot4(float4 a, float4 b, float acc) {
+  return fmaf(a.w, b.w, fmaf(a.z, b.z, fmaf(a.y, b.y, fmaf(a.x, b.x, acc))));
 }
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
@@ -63,13 +71,11 @@ __device__ __forceinline__ int window_rows(const DecodeArgs& a, int b, int& s1, 
 // A CTA serves `per_cta` requests, `rpc` at a time.  Dynamic shared memory: FP32 rows
 // [rpc][nwmax][D + DR], then slot and ring-row indices [rpc][kMaxWindow] (int64) and the row
 // counts [rpc].
-constexpr int kStageLoads = 12;  // staged 16-byte row pieces per thread and chunk (host-checked)
+constexpr int kStageLoads = 24;  // staged 16-byte row pieces per thread and chunk (host-checked)
 
 template <int D, int DR, int H>
 __global__ void __launch_bounds__(THREADS, 1) window_split_kernel(const DecodeArgs a, int rpc, int per_cta) {
   constexpr int KW = D + DR;
-  constexpr int EL = D / 32, RL = DR / 32;  // latent / rope elements per lane
-  static_assert(EL % 4 == 0 && RL >= 1, "lane slices");
   extern __shared__ float4 smem4[];
   const int nwmax = a.cache.sink + a.cache.recent;
   float* rows = reinterpret_cast<float*>(smem4);
@@ -156,68 +162,93 @@ __global__ void __launch_bounds__(THREADS, 1) window_split_kernel(const DecodeAr
     }
   }
   __syncthreads();
-  // -- a warp per (request, head): scores (lane = latent slice), softmax over the rows (lane
-  //    p holds row p), the window partial --
-  for (int pair = warp; pair < rpc * H; pair += THREADS / 32) {
-    const int r = pair / H, h = pair % H, b = b0 + r;
+  // -- a warp per (request, HB heads): lane l holds the latent float4 chunks l + 32 j and the
+  //    rope chunk l (l < DR / 4) of every row, so that a warp's row read is 512 contiguous
+  //    bytes (no bank conflicts) and serves HB heads; scores by warp sums, softmax over the
+  //    rows (lane p holds row p), the window partials --
+  constexpr int HB = D == 512 ? 2 : 4;  // heads per warp
+  constexpr int NCH = D / 128;          // latent float4 chunks per lane
+  constexpr int RCH = DR / 4;           // rope float4 chunks (lanes 0 .. RCH - 1)
+  static_assert(H % HB == 0 && RCH <= 32, "head blocks, rope lanes");
+  for (int item = warp; item < rpc * (H / HB); item += THREADS / 32) {
+    const int r = item / (H / HB), h0 = (item % (H / HB)) * HB, b = b0 + r;
     if (b >= bend) continue;
     const int nw = nwv[r];
-    const uint16_t* qh = a.q + b * a.q_sb + h * a.q_sh;
-    float qv[EL], qr[RL];
+    float4 qv[HB][NCH], qr[HB];
 #pragma unroll
-    for (int c = 0; c < EL / 4; ++c) {
-      const uint2 w = *reinterpret_cast<const uint2*>(qh + EL * lane + 4 * c);
-      qv[4 * c] = __uint_as_float(w.x << 16);
-      qv[4 * c + 1] = __uint_as_float(w.x & 0xFFFF0000u);
-      qv[4 * c + 2] = __uint_as_float(w.y << 16);
-      qv[4 * c + 3] = __uint_as_float(w.y & 0xFFFF0000u);
+    for (int hb = 0; hb < HB; ++hb) {
+      const uint16_t* qh = a.q + b * a.q_sb + (h0 + hb) * a.q_sh;
+#pragma unroll
+      for (int j = 0; j < NCH; ++j) qv[hb][j] = bf16x4(*reinterpret_cast<const uint2*>(qh + 4 * (lane + 32 * j)));
+      qr[hb] = lane < RCH ? bf16x4(*reinterpret_cast<const uint2*>(qh + D + 4 * lane)) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    const float4* rbase = reinterpret_cast<const float4*>(rows + size_t(r) * nwmax * KW);
+    float sp[HB];  // lane p: the score of row p
 #pragma unroll
-    for (int c = 0; c < RL; ++c) qr[c] = __uint_as_float(static_cast<uint32_t>(qh[D + RL * lane + c]) << 16);
-    const float* rbase = rows + size_t(r) * nwmax * KW;
-    float sp = -INFINITY;  // lane p: the score of row p
+    for (int hb = 0; hb < HB; ++hb) sp[hb] = -INFINITY;
     for (int p = 0; p < nw; ++p) {
-      const float* rw = rbase + size_t(p) * KW;
-      float acc = 0.f;
+      const float4* rw = rbase + size_t(p) * (KW / 4);
+      float4 v[NCH];
 #pragma unroll
-      for (int c = 0; c < EL / 4; ++c) {
-        const float4 v = *reinterpret_cast<const float4*>(rw + EL * lane + 4 * c);
-        acc = fmaf(qv[4 * c], v.x, acc);
-        acc = fmaf(qv[4 * c + 1], v.y, acc);
-        acc = fmaf(qv[4 * c + 2], v.z, acc);
-        acc = fmaf(qv[4 * c + 3], v.w, acc);
+      for (int j = 0; j < NCH; ++j) v[j] = rw[lane + 32 * j];
+      const float4 vr = lane < RCH ? rw[D / 4 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+      float acc[HB];
+#pragma unroll
+      for (int hb = 0; hb < HB; ++hb) {
+        float t = dot4(qr[hb], vr, 0.f);
+#pragma unroll
+        for (int j = 0; j < NCH; ++j) t = dot4(qv[hb][j], v[j], t);
+        acc[hb] = t;
       }
 #pragma unroll
-      for (int c = 0; c < RL; ++c) acc = fmaf(qr[c], rw[D + RL * lane + c], acc);
-      acc = warp_sum(acc);
+      for (int o = 16; o >= 1; o >>= 1)
+#pragma unroll
+        for (int hb = 0; hb < HB; ++hb) acc[hb] += __shfl_xor_sync(0xFFFFFFFFu, acc[hb], o);
       // a row whose page is out of range takes no weight (the INT2 splits skip such tokens too)
-      if (lane == p) sp = rslot[r * kMaxWindow + p] >= 0 ? acc * a.sm_scale : -INFINITY;
+      const bool valid = rslot[r * kMaxWindow + p] >= 0;
+#pragma unroll
+      for (int hb = 0; hb < HB; ++hb)
+        if (lane == p) sp[hb] = valid ? acc[hb] * a.sm_scale : -INFINITY;
     }
-    const float m = warp_max(sp);
-    const float e = sp != -INFINITY ? __expf(sp - m) : 0.f;
-    const float l = warp_sum(e);
-    float o[EL];
+    float e[HB], l[HB], m[HB];
 #pragma unroll
-    for (int c = 0; c < EL; ++c) o[c] = 0.f;
+    for (int hb = 0; hb < HB; ++hb) {
+      m[hb] = warp_max(sp[hb]);
+      e[hb] = sp[hb] != -INFINITY ? __expf(sp[hb] - m[hb]) : 0.f;
+      l[hb] = warp_sum(e[hb]);
+    }
+    float4 o[HB][NCH];
+#pragma unroll
+    for (int hb = 0; hb < HB; ++hb)
+#pragma unroll
+      for (int j = 0; j < NCH; ++j) o[hb][j] = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int p = 0; p < nw; ++p) {
-      const float w = __shfl_sync(0xFFFFFFFFu, e, p);
-      const float* rw = rbase + size_t(p) * KW + EL * lane;
+      const float4* rw = rbase + size_t(p) * (KW / 4);
+      float4 v[NCH];
 #pragma unroll
-      for (int c = 0; c < EL / 4; ++c) {
-        const float4 v = *reinterpret_cast<const float4*>(rw + 4 * c);
-        o[4 * c] = fmaf(w, v.x, o[4 * c]);
-        o[4 * c + 1] = fmaf(w, v.y, o[4 * c + 1]);
-        o[4 * c + 2] = fmaf(w, v.z, o[4 * c + 2]);
-        o[4 * c + 3] = fmaf(w, v.w, o[4 * c + 3]);
+      for (int j = 0; j < NCH; ++j) v[j] = rw[lane + 32 * j];
+#pragma unroll
+      for (int hb = 0; hb < HB; ++hb) {
+        const float w = __shfl_sync(0xFFFFFFFFu, e[hb], p);
+#pragma unroll
+        for (int j = 0; j < NCH; ++j) {
+          o[hb][j].x = fmaf(w, v[j].x, o[hb][j].x);
+          o[hb][j].y = fmaf(w, v[j].y, o[hb][j].y);
+          o[hb][j].z = fmaf(w, v[j].z, o[hb][j].z);
+          o[hb][j].w = fmaf(w, v[j].w, o[hb][j].w);
+        }
       }
     }
-    const float il = l > 0.f ? 1.f / l : 0.f;
-    const int64_t row = (static_cast<int64_t>(b) * H + h) * S + a.num_splits;
-    float4* dst = reinterpret_cast<float4*>(a.part_o + row * D + EL * lane);
 #pragma unroll
-    for (int c = 0; c < EL / 4; ++c)
-      dst[c] = make_float4(o[4 * c] * il, o[4 * c + 1] * il, o[4 * c + 2] * il, o[4 * c + 3] * il);
-    if (lane == 0) a.part_lse[row] = l > 0.f ? m + logf(l) : -INFINITY;
+    for (int hb = 0; hb < HB; ++hb) {
+      const float il = l[hb] > 0.f ? 1.f / l[hb] : 0.f;
+      const int64_t row = (static_cast<int64_t>(b) * H + h0 + hb) * S + a.num_splits;
+      float4* dst = reinterpret_cast<float4*>(a.part_o + row * D);
+#pragma unroll
+      for (int j = 0; j < NCH; ++j)
+        dst[lane + 32 * j] = make_float4(o[hb][j].x * il, o[hb][j].y * il, o[hb][j].z * il, o[hb][j].w * il);
+      if (lane == 0) a.part_lse[row] = l[hb] > 0.f ? m[hb] + logf(l[hb]) : -INFINITY;
+    }
   }
   }  // chunk
 }
