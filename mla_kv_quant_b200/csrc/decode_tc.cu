@@ -499,6 +499,18 @@ __global__ void __launch_bounds__(THREADS, 1)
         float2 A[HS / 2], B[HS / 2];
 #pragma unroll
         for (int jp = 0; jp < HS / 2; ++jp) A[jp] = B[jp] = make_float2(0.f, 0.f);
+        // -- 1b. codes of tile i+1 into TMEM (QK^T(i) has completed), in flight together with
+        //        the score loads; once both have landed QK^T(i+1) may start --
+        if (i + 1 < ntiles) {
+#pragma unroll
+          for (int c = 0; c < EW / 16; ++c) {  // 16 columns at a time (register budget)
+            const uint32_t wd[4] = {cw[c].x, cw[c].y, cw[c].z, cw[c].w};
+            uint32_t r[16];
+#pragma unroll
+            for (int kq = 0; kq < 4; ++kq) expand_word(wd[kq], &r[4 * kq]);
+            tmem_st16(tmem + lane_base + C::T_AQK + EW * k + 16 * c, r);
+          }
+        }
         uint32_t pe[HS];
         uint32_t dq[NG][2 * HS];
 #pragma unroll
@@ -509,6 +521,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int g = 0; g < NG; ++g) reg_fence(dq[g]);
         reg_fence(pe);
+        if (i + 1 < ntiles) {
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(&bars[B_AQK]);  // A of QK^T(i+1) is in TMEM, D of QK^T(i) has been read
+        }
 #pragma unroll
         for (int g = 0; g < NG; ++g) {
           const float nscz = -sc[g] * zz[g];
@@ -555,17 +572,6 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       mbar_arrive(&bars[B_PFREE + s]);  // params stage s has been read (sc, zz are in registers)
-      // -- 1b. codes of tile i+1 into TMEM (QK^T(i) has completed) --
-      if (i + 1 < ntiles) {
-#pragma unroll
-        for (int c = 0; c < EW / 16; ++c) {  // 16 columns at a time (register budget)
-          const uint32_t wd[4] = {cw[c].x, cw[c].y, cw[c].z, cw[c].w};
-          uint32_t r[16];
-#pragma unroll
-          for (int kq = 0; kq < 4; ++kq) expand_word(wd[kq], &r[4 * kq]);
-          tmem_st16(tmem + lane_base + C::T_AQK + EW * k + 16 * c, r);
-        }
-      }
       // -- 2. the warp's tile maxima (its 32 tokens) of the HS heads' scores and of the NG
       //       group scales, one redux each, into the head set's table --
       {
@@ -592,13 +598,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // The four warps of head set k (one per token quarter) exchange their maxima; the head
       // sets do not wait for one another.  Each set's group-scale maxima cover all 128 tokens,
       // so every set takes the same E_g decisions.
-      if (i + 1 < ntiles) {  // the 1b stores, waited for after the maxima
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(&bars[B_AQK]);  // A of QK^T(i+1) is in TMEM, D of QK^T(i) has been read
-      } else {
-        tc_fence_before();
-      }
+      tc_fence_before();
       named_bar_sync(4 + k, 128);
       // -- 3. lazy-rescale decisions: lane d = lane & 15 keeps m_ref of head HS k + d (d < HS)
       //       or E of group d - HS in `st`, decides from the head set's table, and the other
