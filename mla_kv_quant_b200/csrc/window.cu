@@ -186,29 +186,42 @@ __global__ void __launch_bounds__(THREADS, 1) window_split_kernel(const DecodeAr
     float sp[HB];  // lane p: the score of row p
 #pragma unroll
     for (int hb = 0; hb < HB; ++hb) sp[hb] = -INFINITY;
-    for (int p = 0; p < nw; ++p) {
-      const float4* rw = rbase + size_t(p) * (KW / 4);
-      float4 v[NCH];
+    // four rows at a time: their warp sums are independent shuffle chains (rows past nw are
+    // zero in shared memory and their scores are dropped; the row index is clamped so that no
+    // read leaves this request's rows)
+    for (int p0 = 0; p0 < nw; p0 += 4) {
+      float acc[4][HB];
 #pragma unroll
-      for (int j = 0; j < NCH; ++j) v[j] = rw[lane + 32 * j];
-      const float4 vr = lane < RCH ? rw[D / 4 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
-      float acc[HB];
+      for (int u = 0; u < 4; ++u) {
+        const float4* rw = rbase + size_t(min(p0 + u, nwmax - 1)) * (KW / 4);
+        float4 v[NCH];
 #pragma unroll
-      for (int hb = 0; hb < HB; ++hb) {
-        float t = dot4(qr[hb], vr, 0.f);
+        for (int j = 0; j < NCH; ++j) v[j] = rw[lane + 32 * j];
+        const float4 vr = lane < RCH ? rw[D / 4 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int j = 0; j < NCH; ++j) t = dot4(qv[hb][j], v[j], t);
-        acc[hb] = t;
+        for (int hb = 0; hb < HB; ++hb) {
+          float t = dot4(qr[hb], vr, 0.f);
+#pragma unroll
+          for (int j = 0; j < NCH; ++j) t = dot4(qv[hb][j], v[j], t);
+          acc[u][hb] = t;
+        }
       }
 #pragma unroll
       for (int o = 16; o >= 1; o >>= 1)
 #pragma unroll
-        for (int hb = 0; hb < HB; ++hb) acc[hb] += __shfl_xor_sync(0xFFFFFFFFu, acc[hb], o);
-      // a row whose page is out of range takes no weight (the INT2 splits skip such tokens too)
-      const bool valid = rslot[r * kMaxWindow + p] >= 0;
+        for (int u = 0; u < 4; ++u)
 #pragma unroll
-      for (int hb = 0; hb < HB; ++hb)
-        if (lane == p) sp[hb] = valid ? acc[hb] * a.sm_scale : -INFINITY;
+          for (int hb = 0; hb < HB; ++hb) acc[u][hb] += __shfl_xor_sync(0xFFFFFFFFu, acc[u][hb], o);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int p = p0 + u;
+        if (p >= nw) break;
+        // a row whose page is out of range takes no weight (the INT2 splits skip such tokens too)
+        const bool valid = rslot[r * kMaxWindow + p] >= 0;
+#pragma unroll
+        for (int hb = 0; hb < HB; ++hb)
+          if (lane == p) sp[hb] = valid ? acc[u][hb] * a.sm_scale : -INFINITY;
+      }
     }
     float e[HB], l[HB], m[HB];
 #pragma unroll
@@ -222,6 +235,7 @@ __global__ void __launch_bounds__(THREADS, 1) window_split_kernel(const DecodeAr
     for (int hb = 0; hb < HB; ++hb)
 #pragma unroll
       for (int j = 0; j < NCH; ++j) o[hb][j] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
     for (int p = 0; p < nw; ++p) {
       const float4* rw = rbase + size_t(p) * (KW / 4);
       float4 v[NCH];
@@ -330,24 +344,24 @@ static int window_rpc(int d, int dr, int nwmax) {
   return max(1, min(rpc, 8));
 }
 
-// The window-first launch applies when the INT2 grid and one window CTA per rpc requests fit
-// on the SMs together: no INT2 CTA then waits for a window CTA (measured at B128 x 8K with
-// D = 512, window CTAs looping over two chunks on the 20 free SMs: 226 against 206 us per
-// layer for the window split after the INT2 kernel).
+// The window-first launch applies when the INT2 grid is one wave and leaves SMs free for the
+// window CTAs, each looping over at most two chunks of rpc requests: the window grid then
+// stays shorter than the INT2 kernel (B128 x 8K, D = 512, 1 split: 20 window CTAs, two chunks
+// each: 176 against 188 us per layer for the window split after the INT2 kernel).
 bool window_first_fits(const DecodeArgs& a) {
   const int rpc = window_rpc(a.cache.latent_dim, a.cache.rope_dim, a.cache.sink + a.cache.recent);
-  return int64_t(a.batch) * a.num_splits + (a.batch + rpc - 1) / rpc <= sm_count();
+  const int64_t free_sms = sm_count() - int64_t(a.batch) * a.num_splits;
+  return free_sms >= 1 && free_sms * 2 * rpc >= a.batch;
 }
 
-// CTAs: only as many as the SMs the INT2 grid leaves free (its CTAs hold a whole SM each),
+// CTAs: at most max_ctas (the SMs the INT2 grid leaves free: its CTAs hold a whole SM each),
 // each looping over its requests rpc at a time.
 template <int D, int DR, int H>
-static int launch_window_split(const DecodeArgs& a, cudaStream_t s) {
+static int launch_window_split(const DecodeArgs& a, int max_ctas, cudaStream_t s) {
   const int nwmax = a.cache.sink + a.cache.recent;
   const size_t per_req = size_t(nwmax) * (D + DR) * 4 + 2 * win::kMaxWindow * 8 + 4;
   const int rpc = window_rpc(D, DR, nwmax);
-  const int free_sms = max(1, sm_count() - a.batch * a.num_splits);
-  const int ctas = max(1, min((a.batch + rpc - 1) / rpc, free_sms));
+  const int ctas = max(1, min((a.batch + rpc - 1) / rpc, max_ctas));
   const int per_cta = (a.batch + ctas - 1) / ctas;
   const size_t smem = size_t(rpc) * per_req + 16;
   static const bool attr = cudaFuncSetAttribute(win::window_split_kernel<D, DR, H>,
@@ -376,19 +390,29 @@ static int launch_merge_splits(const DecodeArgs& a, int heads, uint16_t* out, in
   return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;
 }
 
-int launch_decode_windowed(const DecodeArgs& a, int heads, uint16_t* out, int64_t out_sb, int64_t out_sh,
-                           float* out_lse, cudaStream_t s) {
+// The window split on win_ctas CTAs, then the INT2 kernel (grid as `a` says) and the merge as
+// programmatic dependents.
+static int launch_window_first(const DecodeArgs& a, int win_ctas, int heads, uint16_t* out, int64_t out_sb,
+                               int64_t out_sh, float* out_lse, cudaStream_t s) {
   const int d = a.cache.latent_dim;
   int rc;
   if (d == 512)
-    rc = heads == 16 ? launch_window_split<512, 64, 16>(a, s) : launch_window_split<512, 64, 8>(a, s);
+    rc = heads == 16 ? launch_window_split<512, 64, 16>(a, win_ctas, s)
+                     : launch_window_split<512, 64, 8>(a, win_ctas, s);
   else
-    rc = heads == 40 ? launch_window_split<256, 32, 40>(a, s) : launch_window_split<256, 32, 16>(a, s);
+    rc = heads == 40 ? launch_window_split<256, 32, 40>(a, win_ctas, s)
+                     : launch_window_split<256, 32, 16>(a, win_ctas, s);
   if (rc != ROLAQ_OK) return rc;
   rc = launch_decode_tc(a, heads, s, true);
   if (rc != ROLAQ_OK) return rc;
   return d == 512 ? launch_merge_splits<512>(a, heads, out, out_sb, out_sh, out_lse, s)
                   : launch_merge_splits<256>(a, heads, out, out_sb, out_sh, out_lse, s);
 }
+
+int launch_decode_windowed(const DecodeArgs& a, int heads, uint16_t* out, int64_t out_sb, int64_t out_sh,
+                           float* out_lse, cudaStream_t s) {
+  return launch_window_first(a, max(1, sm_count() - a.batch * a.num_splits), heads, out, out_sb, out_sh, out_lse, s);
+}
+
 
 }  // namespace rolaq

@@ -172,3 +172,33 @@ def test_decode_minicpm3_shape_default_splits(which):
         assert np.max(np.abs(o[i] - ref[i]) - half_ulp) <= 2e-2, f"request {i}"
         assert cosine(o[i], ref[i]) >= 0.9995
 
+
+
+def test_decode_window_ctas_loop_over_chunks():
+    """B = 128 with one split (the Moonlight layout): the INT2 grid leaves 20 SMs, so each
+    window CTA serves two chunks of requests while the INT2 kernel runs; a seeded subset of
+    requests against the FP64 oracle."""
+    d, dr, h, b, ctx = 512, 64, 16, 128, 640
+    seq_lens = [ctx - 7 * (i % 5) for i in range(b)]
+    g = torch.Generator().manual_seed(71)
+    pages = (ctx + 63) // 64
+    pt = (torch.randperm(b * pages, generator=g) + 1).to(torch.int32).reshape(b, pages).cuda()
+    pool = GpuPool(64 * (b * pages + 1), d, dr, max_reqs=b, sink=4, recent=16)
+    fill_requests(pool, seq_lens, pt, synth.rotation(d, seed=72), ops.codec_serving(0.85, synth.signal_gain(0.85)),
+                  seed=73)
+    q = synth.normal_bf16((b, h, d + dr), seed=74, device="cuda")
+    sl = torch.tensor(seq_lens, dtype=torch.int32, device="cuda")
+    out = torch.full((b, h, d), float("nan"), dtype=torch.bfloat16, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    sm = 1.0 / np.sqrt(192.0)
+    ops.packed_decode(q, pool.view(), pt, sl, sm, 1, torch.empty(b, h, 2, d, device="cuda"),
+                      torch.empty(b, h, 2, device="cuda"), out, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    sub = sorted(np.random.default_rng(75).choice(b, size=10, replace=False).tolist() + [0, b - 1])
+    ref, _ = odecode.decode(pool.to_oracle(), bits(q), pt.cpu().numpy(), seq_lens, sm, requests=sub)
+    o = out.float().cpu().numpy()
+    for i in sub:
+        half_ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(ref[i]), 1e-30))) - 8)
+        assert np.max(np.abs(o[i] - ref[i]) - half_ulp) <= 2e-2, f"request {i}"
+        assert cosine(o[i], ref[i]) >= 0.9995

@@ -177,16 +177,21 @@ def test_decode_token_range_partials_merge_to_full():
     merged = torch.empty(b * h, d, device="cuda")
     ops.merge_partials(torch.stack(outs), torch.stack(lses), out_f32=merged)
     torch.cuda.synchronize()
-    # Slicing the sequence moves the tile boundaries that the attention weights are
-    # quantised against (two E4M3 terms: ~2^-9 relative per weight, the precision of
-    # the BF16 weights in the reference's P.V), so the two FP32 results agree to the
-    # weight precision, not bit for bit; both are checked against the oracle as well.
+    # Both results against the FP64 oracle (the decode tolerance), then against each other.
+    # Slicing the sequence moves the tile (and segment) boundaries that the attention weights
+    # are quantised against: two E4M3 terms carry a weight to 2^-8 of itself, so the two FP32
+    # results agree to 2^-8 of the largest dequantised value a weight multiplies, not bit for bit.
     merged_np = merged.view(b, h, d).cpu().numpy()
-    diff = np.abs(merged_np - full32).max()
-    assert diff <= 4e-3
     ref, _ = odecode.decode(pool.to_oracle(), bits(q), pt.cpu().numpy(), seq_lens, 0.07)
     for i in range(b):
-        assert np.abs(merged_np[i] - ref[i]).max() <= 2e-2
+        e_full = np.abs(full32[i] - ref[i]).max()
+        e_merged = np.abs(merged_np[i] - ref[i]).max()
+        print(f"request {i}: full vs oracle {e_full:.3g}, slices vs oracle {e_merged:.3g}, "
+              f"max |ref| {np.abs(ref[i]).max():.3g}")
+        assert e_full <= 2e-2 and e_merged <= 2e-2
+    diff = np.abs(merged_np - full32).max()
+    print(f"slices vs full: {diff:.3g}")
+    assert diff <= 1e-2
 
 
 def test_decode_bad_page_is_reported():
