@@ -412,18 +412,23 @@ def run_ours(args, rank, world, dev):
                 "eager": {"value": world * batch / e2e_eager_s, "unit": "tok/s", "ms_per_step": e2e_eager_s * 1e3,
                           "path": "the same calls and copies launched eagerly every step"},
                 "absorbed": e2e_abs},
-        "roofline": {"kernel": "rolaq decode (decode_tc_kernel + merge_window_kernel), one layer", "bound": "hbm",
+        "roofline": {"kernel": "rolaq decode call, one layer (window_split_kernel, decode_tc_kernel and "
+                               "merge_splits_kernel when the INT2 grid is one wave, else decode_tc_kernel and "
+                               "merge_window_kernel)", "bound": "hbm",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_source": f"{peak_kind} hbm_gbs", "traffic": traffic, "traffic_source": traffic_src,
                      "algorithmic_bytes_per_launch": dbytes, "launch_us": dec_s * 1e6},
         "writer": {"rows_per_launch": wrows, "launch_us": w_s * 1e6, "gbs": w_bytes / w_s / 1e9,
                    "hbm_frac": (w_bytes / w_s / 1e9) / hbm, "tflops": w_flops / w_s / 1e12,
                    "tensor_frac": (w_flops / w_s / 1e12) / tf_burst,
+                   "tensor_frac_sustained": (w_flops / w_s / 1e12) / tf_sus,
                    "roofline_frac": max(w_bytes / (hbm * 1e9), w_flops / (tf_burst * 1e12)) / w_s,
                    "bound": "tensor" if w_flops / (tf_burst * 1e12) > w_bytes / (hbm * 1e9) else "hbm",
                    "note": "roofline_frac = max(bytes/HBM peak, flops/bf16 peak) / time, of " + peak_kind},
         "clocks": clocks,
-        "gpu_launches": args.steps * LAYERS * 3,  # per layer: fused writer, decode_tc, merge_window
+        # per layer: the fused writer, then window_split + decode_tc + merge_splits (one-wave INT2
+        # grid) or decode_tc + merge_window
+        "gpu_launches": args.steps * LAYERS * (4 if batch * splits < 148 else 3),
         "gpus_active": world,
     }
     return res
