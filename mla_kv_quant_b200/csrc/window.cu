@@ -71,7 +71,7 @@ __device__ __forceinline__ int window_rows(const DecodeArgs& a, int b, int& s1, 
 // A CTA serves `per_cta` requests, `rpc` at a time.  Dynamic shared memory: FP32 rows
 // [rpc][nwmax][D + DR], then slot and ring-row indices [rpc][kMaxWindow] (int64) and the row
 // counts [rpc].
-constexpr int kStageLoads = 24;  // staged 16-byte row pieces per thread and chunk (host-checked)
+constexpr int kStageLoads = 12;  // staged 16-byte row pieces per thread and chunk (host-checked)
 
 template <int D, int DR, int H>
 __global__ void __launch_bounds__(THREADS, 1) window_split_kernel(const DecodeArgs a, int rpc, int per_cta) {
@@ -116,26 +116,27 @@ __global__ void __launch_bounds__(THREADS, 1) window_split_kernel(const DecodeAr
     rrow[idx] = rr;
   }
   __syncthreads();
-  // -- the rows into shared memory as FP32, four values per thread and step: latent values
+  // -- the rows into shared memory as FP32, eight values per thread and step: latent values
   //    from the BF16 ring row or (ring row taken over) (code - zero) * scale, rope values
   //    from k_pe; absent rows stay zero --
-  constexpr int C4 = KW / 4;
+  constexpr int C8 = KW / 8;
+  static_assert(KW % 8 == 0 && D % 8 == 0, "16-byte row pieces");
   {
     // every load of the thread is issued before any is used (one round trip per chunk)
-    const int total = rpc * nwmax * C4;
-    uint2 raw[kStageLoads];
+    const int total = rpc * nwmax * C8;
+    uint4 raw[kStageLoads];
 #pragma unroll
     for (int k = 0; k < kStageLoads; ++k) {
       const int idx = tid + k * THREADS;
-      raw[k] = make_uint2(0, 0);
+      raw[k] = make_uint4(0, 0, 0, 0);
       if (idx < total) {
-        const int r = idx / (nwmax * C4), rem = idx % (nwmax * C4), p = rem / C4, e4 = 4 * (rem % C4);
+        const int row = idx / C8, e8 = 8 * (idx % C8), r = row / nwmax, p = row % nwmax;
         const int64_t slot = rslot[r * kMaxWindow + p], rr = rrow[r * kMaxWindow + p];
         if (p < nwv[r] && slot >= 0) {
-          if (e4 >= D)
-            raw[k] = *reinterpret_cast<const uint2*>(a.cache.rope + slot * DR + (e4 - D));
+          if (e8 >= D)
+            raw[k] = *reinterpret_cast<const uint4*>(a.cache.rope + slot * DR + (e8 - D));
           else if (rr >= 0)
-            raw[k] = *reinterpret_cast<const uint2*>(a.cache.hp + rr * D + e4);
+            raw[k] = *reinterpret_cast<const uint4*>(a.cache.hp + rr * D + e8);
         }
       }
     }
@@ -143,22 +144,30 @@ __global__ void __launch_bounds__(THREADS, 1) window_split_kernel(const DecodeAr
     for (int k = 0; k < kStageLoads; ++k) {
       const int idx = tid + k * THREADS;
       if (idx >= total) continue;
-      const int r = idx / (nwmax * C4), rem = idx % (nwmax * C4), p = rem / C4, e4 = 4 * (rem % C4);
+      const int row = idx / C8, e8 = 8 * (idx % C8), r = row / nwmax, p = row % nwmax;
       const int64_t slot = rslot[r * kMaxWindow + p], rr = rrow[r * kMaxWindow + p];
-      float4 v;
-      if (p < nwv[r] && slot >= 0 && e4 < D && rr < 0) {  // ring row taken over (rare): the INT2 codes
-        const uint32_t cb = a.cache.codes[slot * (D / 4) + e4 / 4];
-        const float2 sz = reinterpret_cast<const float2*>(a.cache.params)[slot * (D / 128) + e4 / 128];
-        v = make_float4(__fmul_rn(__fsub_rn(static_cast<float>(cb & 3u), sz.y), sz.x),
-                        __fmul_rn(__fsub_rn(static_cast<float>((cb >> 2) & 3u), sz.y), sz.x),
-                        __fmul_rn(__fsub_rn(static_cast<float>((cb >> 4) & 3u), sz.y), sz.x),
-                        __fmul_rn(__fsub_rn(static_cast<float>((cb >> 6) & 3u), sz.y), sz.x));
+      float4 v[2];
+      if (p < nwv[r] && slot >= 0 && e8 < D && rr < 0) {  // ring row taken over (rare): the INT2 codes
+        const uint32_t cw = *reinterpret_cast<const uint16_t*>(a.cache.codes + slot * (D / 4) + e8 / 4);
+        const float2 sz = reinterpret_cast<const float2*>(a.cache.params)[slot * (D / 128) + e8 / 128];
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const uint32_t cb = cw >> (8 * h2);
+          v[h2] = make_float4(__fmul_rn(__fsub_rn(static_cast<float>(cb & 3u), sz.y), sz.x),
+                              __fmul_rn(__fsub_rn(static_cast<float>((cb >> 2) & 3u), sz.y), sz.x),
+                              __fmul_rn(__fsub_rn(static_cast<float>((cb >> 4) & 3u), sz.y), sz.x),
+                              __fmul_rn(__fsub_rn(static_cast<float>((cb >> 6) & 3u), sz.y), sz.x));
+        }
       } else {  // BF16 (ring row or k_pe); absent rows stay zero
-        const uint2 w = raw[k];
-        v = make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xFFFF0000u), __uint_as_float(w.y << 16),
-                        __uint_as_float(w.y & 0xFFFF0000u));
+        const uint4 w = raw[k];
+        v[0] = make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xFFFF0000u), __uint_as_float(w.y << 16),
+                           __uint_as_float(w.y & 0xFFFF0000u));
+        v[1] = make_float4(__uint_as_float(w.z << 16), __uint_as_float(w.z & 0xFFFF0000u), __uint_as_float(w.w << 16),
+                           __uint_as_float(w.w & 0xFFFF0000u));
       }
-      reinterpret_cast<float4*>(rows)[(size_t(r) * nwmax + p) * C4 + e4 / 4] = v;
+      float4* dst = reinterpret_cast<float4*>(rows) + (size_t(r) * nwmax + p) * (KW / 4) + e8 / 4;
+      dst[0] = v[0];
+      dst[1] = v[1];
     }
   }
   __syncthreads();
@@ -340,7 +349,7 @@ static int window_rpc(int d, int dr, int nwmax) {
   if (nwmax <= 0) return 8;
   const size_t per_req = size_t(nwmax) * (d + dr) * 4 + 2 * win::kMaxWindow * 8 + 4;
   int rpc = static_cast<int>((200 * 1024) / per_req);
-  rpc = min(rpc, (win::kStageLoads * win::THREADS) / (nwmax * (d + dr) / 4));
+  rpc = min(rpc, (win::kStageLoads * win::THREADS) / (nwmax * (d + dr) / 8));
   return max(1, min(rpc, 8));
 }
 
@@ -363,12 +372,13 @@ static int launch_window_split(const DecodeArgs& a, int max_ctas, cudaStream_t s
   const int rpc = window_rpc(D, DR, nwmax);
   const int ctas = max(1, min((a.batch + rpc - 1) / rpc, max_ctas));
   const int per_cta = (a.batch + ctas - 1) / ctas;
-  const size_t smem = size_t(rpc) * per_req + 16;
+  const int rpc_run = min(rpc, per_cta);  // a chunk never covers more requests than the CTA serves
+  const size_t smem = size_t(rpc_run) * per_req + 16;
   static const bool attr = cudaFuncSetAttribute(win::window_split_kernel<D, DR, H>,
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 (int)(208 * 1024)) == cudaSuccess;
   if (!attr) return ROLAQ_ECUDA;
-  win::window_split_kernel<D, DR, H><<<static_cast<unsigned>(ctas), win::THREADS, smem, s>>>(a, rpc, per_cta);
+  win::window_split_kernel<D, DR, H><<<static_cast<unsigned>(ctas), win::THREADS, smem, s>>>(a, rpc_run, per_cta);
   return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;
 }
 
