@@ -995,12 +995,73 @@ def run_seqsplit(args, rank, world, dev):
     torch.cuda.synchronize()
     del graph  # before the process group goes: the graph holds the NCCL call
     g_us = sorted(gl)[len(gl) // 2]
-    t = torch.tensor([k_us, c_us, k_us + c_us, g_us], device=dev)
+
+    # The same layer with the partials exchanged over NVLink peer memory (PeerExchange): the
+    # slice's splits are merged and written into every rank's receive buffer by one kernel,
+    # and the final merge waits for every rank's partial; eager and graph-replayed.  The
+    # output is compared with the NCCL path's (max abs difference of the BF16 outputs).
+    from mla_kv_quant_b200.seqsplit import PeerExchange
+
+    if world > 1:
+        ref32, _ = gather_merge(o_loc, lse_loc)
+    else:
+        ref32 = o_loc.clone()
+    ref = ref32.to(torch.bfloat16).view(1, HEADS, D)
+    xch = PeerExchange(HEADS, D, device=dev)
+    out_p = torch.empty(1, HEADS, D, dtype=torch.bfloat16, device=dev)
+    perr = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def layer_peer():
+        ops.packed_decode(q, view, pt, sl, sm, splits, part_o, part_lse, None, token_range=rng)
+        xch.exchange(part_o, part_lse, out_bf16=out_p, err=perr)
+
+    pl = []
+    for it in range(args.warmup + args.steps):
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        ev[0].record()
+        layer_peer()
+        ev[2].record()
+        torch.cuda.synchronize()
+        if it >= args.warmup:
+            pl.append(ev[0].elapsed_time(ev[2]) * 1e3)
+    peer_diff = float((out_p.float() - ref.float()).abs().max())
+    with torch.cuda.stream(side):
+        layer_peer()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        layer_peer()
+    pg = []
+    for it in range(args.warmup + args.steps):
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        ev[0].record()
+        graph.replay()
+        ev[2].record()
+        torch.cuda.synchronize()
+        if it >= args.warmup:
+            pg.append(ev[0].elapsed_time(ev[2]) * 1e3)
+    del graph
+    peer_err = int(perr.item())
+    xch.close()
+    p_us, pg_us = sorted(pl)[len(pl) // 2], sorted(pg)[len(pg) // 2]
+
+    t = torch.tensor([k_us, c_us, k_us + c_us, g_us, p_us, pg_us, peer_diff, float(peer_err)], device=dev)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     return {"mode": "seqsplit", "n_gpus": world, "batch": 1, "ctx": ctx, "tokens_per_rank": n,
             "num_splits_per_rank": splits, "us_per_layer": float(t[2]), "kernel_us": float(t[0]),
             "gather_merge_us": float(t[1]), "us_per_layer_graph": float(t[3]),
+            "peer": {"us_per_layer": float(t[4]), "us_per_layer_graph": float(t[5]),
+                     "max_abs_diff_vs_nccl": float(t[6]), "err_bits": int(t[7]),
+                     "path": "the slice's split partials (window split + INT2 kernel, no merge) + one kernel that "
+                             "merges them and writes the FP32 partial into every rank's receive buffer over "
+                             "NVLink (CUDA IPC) + a merge that waits for every rank's partial; no library "
+                             "collective"},
             "note": "median over steps of each rank, max over ranks; kernel = the slice's decode call (INT2 "
                     "splits + window + merge) and its FP32 partial merge, gather_merge = one NCCL "
                     "all-gather of the (o, lse) partials + the merge kernel (eager launches); "

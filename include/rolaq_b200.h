@@ -43,6 +43,7 @@ extern "C" {
 #define ROLAQ_DEV_BAD_PAGE 2    /* a page index outside the pool was skipped */
 #define ROLAQ_DEV_TIMEOUT 4     /* a bounded wait on an mbarrier gave up */
 #define ROLAQ_DEV_BAD_REQ 8     /* seq_len larger than the page table allows */
+#define ROLAQ_DEV_PEER_TIMEOUT 16 /* a bounded wait for another rank's partial gave up */
 
 /* One layer of the packed cache plus the shared slot/ring maps. */
 typedef struct rolaq_layer_cache {
@@ -185,6 +186,8 @@ int rolaq_prepare_gf_splits(const int32_t* splits, int32_t* quant, int32_t* merg
  *   part_o     f32 [B, H, num_splits + 1, D]  scratch (the reference's attn_logits)
  *   part_lse   f32 [B, H, num_splits + 1]     scratch (the reference's attn_lse)
  *   out        bf16 [B, H, D] with strides (out_stride_b, out_stride_h)
+ *              (NULL: only the split partials are written, the window split's at index
+ *              num_splits, for a caller that merges them itself, e.g. across ranks)
  * Supported: H = 16 with D = 512, Dr = 64; H = 40 with D = 256, Dr = 32 (any H that
  * is a multiple of 8 up to 64 with D in {256, 512}).
  */
@@ -277,6 +280,40 @@ int rolaq_merge_partials(const float* part_o, int64_t row_stride, int64_t part_s
                          const float* part_lse, int64_t lse_row_stride, int64_t lse_part_stride,
                          int32_t n_parts, int64_t rows, int32_t latent_dim, uint16_t* out_bf16,
                          float* out_f32, int64_t ld_out, float* out_lse, cudaStream_t stream);
+
+/*
+ * Sequence-split exchange over NVLink peer memory (no counterpart in the reference, which
+ * serves one GPU: deployment/serve.py:135-136; the merge is the split-KV LSE merge of
+ * packed_mla_decode_gf_fwd, deployment/patches/rolaq_sglang.patch:98-111).  Each rank of a
+ * sequence-split decode owns a receive buffer of rolaq_peer_recv_bytes bytes (allocated with
+ * rolaq_device_alloc, zeroed, and mapped into every other rank with the CUDA IPC helpers)
+ * and a zeroed int32 state[2] of its own.  Per decode, on every rank in the same order:
+ *   rolaq_peer_merge_push  merges the rank's split partials (the part_o / part_lse scratch of
+ *                          a token-range rolaq_packed_decode) in FP32 and writes the result
+ *                          into every rank's receive buffer (peer_recv: device array of the
+ *                          world buffer addresses as mapped in this process), then flags it;
+ *   rolaq_peer_wait_merge  waits (bounded: ROLAQ_DEV_PEER_TIMEOUT after ~2 s) until every
+ *                          rank's partial has arrived and LSE-merges them into out.
+ * rows = batch * heads; latent_dim 256 or 512.  The state and flags live on the device, so
+ * the two calls may be captured in a CUDA graph and replayed.
+ */
+int64_t rolaq_peer_recv_bytes(int32_t world, int64_t rows, int32_t latent_dim);
+int rolaq_peer_merge_push(const float* part_o, const float* part_lse, int32_t n_parts, int64_t rows,
+                          int32_t latent_dim, const uint64_t* peer_recv, int32_t world, int32_t rank,
+                          int32_t* state, cudaStream_t stream);
+int rolaq_peer_wait_merge(const float* recv, int32_t world, int64_t rows, int32_t latent_dim,
+                          const int32_t* state, uint16_t* out_bf16, float* out_f32, float* out_lse,
+                          int32_t* err, cudaStream_t stream);
+
+/* Device buffers for the exchange (cudaMalloc of the current device, zero-filled before the
+ * call returns; cudaFree) and their CUDA IPC mappings: a handle is ROLAQ_IPC_HANDLE_BYTES
+ * opaque bytes. */
+#define ROLAQ_IPC_HANDLE_BYTES 64
+int rolaq_device_alloc(int64_t bytes, void** ptr);
+int rolaq_device_free(void* ptr);
+int rolaq_ipc_get_handle(const void* ptr, void* handle);
+int rolaq_ipc_open(const void* handle, void** ptr);
+int rolaq_ipc_close(void* ptr);
 
 #ifdef __cplusplus
 }

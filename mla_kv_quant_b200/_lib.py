@@ -27,6 +27,8 @@ DEV_BAD_SLOT = 1
 DEV_BAD_PAGE = 2
 DEV_TIMEOUT = 4
 DEV_BAD_REQ = 8
+DEV_PEER_TIMEOUT = 16
+IPC_HANDLE_BYTES = 64
 
 EXPORTS = (
     "rolaq_version",
@@ -45,6 +47,14 @@ EXPORTS = (
     "rolaq_absorb_query",
     "rolaq_project_output",
     "rolaq_page_table_from_req_to_token",
+    "rolaq_peer_recv_bytes",
+    "rolaq_peer_merge_push",
+    "rolaq_peer_wait_merge",
+    "rolaq_device_alloc",
+    "rolaq_device_free",
+    "rolaq_ipc_get_handle",
+    "rolaq_ipc_open",
+    "rolaq_ipc_close",
 )
 
 
@@ -120,6 +130,14 @@ _SIGS = {
     "rolaq_page_table_from_req_to_token": (INT, [P, I64, P, INT, P, INT, I64, I32, P, I64, P, P, P]),
     "rolaq_absorb_query": (INT, [P, I64, I64, P, I64, I64, P, I32, I32, I32, I32, I32, P, I64, I64, P, P]),
     "rolaq_project_output": (INT, [P, I64, I64, P, I32, I32, I32, I32, P, I64, I64, P, P]),
+    "rolaq_peer_recv_bytes": (I64, [I32, I64, I32]),
+    "rolaq_peer_merge_push": (INT, [P, P, I32, I64, I32, P, I32, I32, P, P]),
+    "rolaq_peer_wait_merge": (INT, [P, I32, I64, I32, P, P, P, P, P, P]),
+    "rolaq_device_alloc": (INT, [I64, ctypes.POINTER(ctypes.c_void_p)]),
+    "rolaq_device_free": (INT, [P]),
+    "rolaq_ipc_get_handle": (INT, [P, P]),
+    "rolaq_ipc_open": (INT, [P, ctypes.POINTER(ctypes.c_void_p)]),
+    "rolaq_ipc_close": (INT, [P]),
 }
 
 

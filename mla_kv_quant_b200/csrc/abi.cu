@@ -3,6 +3,7 @@
 // status code, and records a message for rolaq_last_error() on failure.
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 
 #include "kernels.cuh"
@@ -228,13 +229,14 @@ int rolaq_packed_decode(const uint16_t* q, int64_t q_stride_b, int64_t q_stride_
   if (!(sm_scale > 0.f)) return fail(ROLAQ_EINVAL, "sm_scale must be > 0");
   if (batch == 0) return ROLAQ_OK;
   if (batch > 65535) return fail(ROLAQ_EINVAL, "batch must be <= 65535");
-  if (!q || !page_table || !seq_lens || !part_o || !part_lse || !out) return fail(ROLAQ_EINVAL, "NULL pointer");
+  if (!q || !page_table || !seq_lens || !part_o || !part_lse) return fail(ROLAQ_EINVAL, "NULL pointer");
   if (max_pages <= 0 || pt_stride < max_pages) return fail(ROLAQ_EINVAL, "page table shape");
   if (q_stride_h < d + cache->rope_dim || q_stride_b < heads * q_stride_h)
     return fail(ROLAQ_EINVAL, "q strides too small");
   if ((reinterpret_cast<uintptr_t>(q) & 3) || (q_stride_h & 1) || (q_stride_b & 1))
     return fail(ROLAQ_EINVAL, "q must be 4-byte aligned with even strides");
-  if (out_stride_h < d || out_stride_b < heads * out_stride_h) return fail(ROLAQ_EINVAL, "out strides too small");
+  if (out && (out_stride_h < d || out_stride_b < heads * out_stride_h))
+    return fail(ROLAQ_EINVAL, "out strides too small");
   DecodeArgs a{};
   a.q = q;
   a.q_sb = q_stride_b;
@@ -251,6 +253,7 @@ int rolaq_packed_decode(const uint16_t* q, int64_t q_stride_b, int64_t q_stride_
   a.part_o = part_o;
   a.part_lse = part_lse;
   a.err = err;
+  if (!out) return cuda_rc(launch_decode_partials(a, heads, stream), "packed_decode");  // the partials only
   {
     const int fused = launch_decode_merged(a, heads, out, out_stride_b, out_stride_h, out_lse, stream);
     if (fused != ROLAQ_EUNSUPPORTED) return cuda_rc(fused, "packed_decode");
@@ -273,6 +276,80 @@ int rolaq_packed_decode(const uint16_t* q, int64_t q_stride_b, int64_t q_stride_
     if (rc != ROLAQ_OK) return rc;
   }
   return ROLAQ_OK;
+}
+
+int64_t rolaq_peer_recv_bytes(int32_t world, int64_t rows, int32_t latent_dim) {
+  if (world < 1 || rows < 0 || (latent_dim != 256 && latent_dim != 512)) return -1;
+  return peer_recv_bytes(world, rows, latent_dim);
+}
+
+int rolaq_peer_merge_push(const float* part_o, const float* part_lse, int32_t n_parts, int64_t rows,
+                          int32_t latent_dim, const uint64_t* peer_recv, int32_t world, int32_t rank, int32_t* state,
+                          cudaStream_t stream) {
+  if (latent_dim != 256 && latent_dim != 512) return fail(ROLAQ_EUNSUPPORTED, "latent_dim must be 256 or 512");
+  if (world < 1 || world > 64 || rank < 0 || rank >= world) return fail(ROLAQ_EINVAL, "rank / world out of range");
+  if (n_parts < 1 || rows < 0 || rows > (1 << 24)) return fail(ROLAQ_EINVAL, "n_parts < 1 or rows out of range");
+  if (rows == 0) return ROLAQ_OK;
+  if (!part_o || !part_lse || !peer_recv || !state) return fail(ROLAQ_EINVAL, "NULL pointer");
+  if (reinterpret_cast<uintptr_t>(part_o) & 15) return fail(ROLAQ_EINVAL, "part_o must be 16-byte aligned");
+  return cuda_rc(launch_peer_merge_push(part_o, part_lse, n_parts, static_cast<int>(rows), latent_dim, peer_recv, world,
+                                        rank, state, stream),
+                 "peer_merge_push");
+}
+
+int rolaq_peer_wait_merge(const float* recv, int32_t world, int64_t rows, int32_t latent_dim, const int32_t* state,
+                          uint16_t* out_bf16, float* out_f32, float* out_lse, int32_t* err, cudaStream_t stream) {
+  if (latent_dim != 256 && latent_dim != 512) return fail(ROLAQ_EUNSUPPORTED, "latent_dim must be 256 or 512");
+  if (world < 1 || world > 64 || rows < 0 || rows > (1 << 24)) return fail(ROLAQ_EINVAL, "world / rows out of range");
+  if (rows == 0) return ROLAQ_OK;
+  if (!recv || !state) return fail(ROLAQ_EINVAL, "NULL pointer");
+  if ((reinterpret_cast<uintptr_t>(recv) & 15) || (reinterpret_cast<uintptr_t>(out_bf16) & 15) ||
+      (reinterpret_cast<uintptr_t>(out_f32) & 15))
+    return fail(ROLAQ_EINVAL, "recv and outputs must be 16-byte aligned");
+  return cuda_rc(launch_peer_wait_merge(recv, world, static_cast<int>(rows), latent_dim, state, out_bf16, out_f32,
+                                        out_lse, err, stream),
+                 "peer_wait_merge");
+}
+
+int rolaq_device_alloc(int64_t bytes, void** ptr) {
+  if (!ptr || bytes <= 0) return fail(ROLAQ_EINVAL, "bytes must be > 0 and ptr non-NULL");
+  *ptr = nullptr;
+  if (cudaMalloc(ptr, static_cast<size_t>(bytes)) != cudaSuccess) return cuda_rc(ROLAQ_ECUDA, "device_alloc");
+  if (cudaMemset(*ptr, 0, static_cast<size_t>(bytes)) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return cuda_rc(ROLAQ_ECUDA, "device_alloc");
+  }
+  return ROLAQ_OK;
+}
+
+int rolaq_device_free(void* ptr) {
+  if (!ptr) return ROLAQ_OK;
+  return cuda_rc(cudaFree(ptr) == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA, "device_free");
+}
+
+int rolaq_ipc_get_handle(const void* ptr, void* handle) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == ROLAQ_IPC_HANDLE_BYTES, "IPC handle size");
+  if (!ptr || !handle) return fail(ROLAQ_EINVAL, "NULL pointer");
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, const_cast<void*>(ptr)) != cudaSuccess) return cuda_rc(ROLAQ_ECUDA, "ipc_get_handle");
+  memcpy(handle, &h, sizeof(h));
+  return ROLAQ_OK;
+}
+
+int rolaq_ipc_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return fail(ROLAQ_EINVAL, "NULL pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  *ptr = nullptr;
+  if (cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+    return cuda_rc(ROLAQ_ECUDA, "ipc_open");
+  return ROLAQ_OK;
+}
+
+int rolaq_ipc_close(void* ptr) {
+  if (!ptr) return ROLAQ_OK;
+  return cuda_rc(cudaIpcCloseMemHandle(ptr) == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA, "ipc_close");
 }
 
 int rolaq_merge_partials(const float* part_o, int64_t row_stride, int64_t part_stride, const float* part_lse,

@@ -99,6 +99,12 @@ int launch_decode(const DecodeArgs& a, int heads, cudaStream_t s);
 // 512/64/16, aligned output); ROLAQ_EUNSUPPORTED otherwise (nothing launched).
 int launch_decode_merged(const DecodeArgs& a, int heads, uint16_t* out, int64_t out_sb, int64_t out_sh,
                          float* out_lse, cudaStream_t s);
+int64_t peer_recv_bytes(int world, int64_t rows, int d);
+int launch_decode_partials(const DecodeArgs& a, int heads, cudaStream_t s);
+int launch_peer_merge_push(const float* part_o, const float* part_lse, int n_parts, int rows, int d,
+                           const uint64_t* peers, int world, int rank, int32_t* state, cudaStream_t s);
+int launch_peer_wait_merge(const float* recv, int world, int rows, int d, const int32_t* state, uint16_t* out_bf16,
+                           float* out_f32, float* out_lse, int32_t* err, cudaStream_t s);
 int launch_merge(const float* part_o, int64_t row_stride, int64_t part_stride, const float* part_lse,
                  int64_t lse_row_stride, int64_t lse_part_stride, int n_parts, int64_t rows, int d,
                  uint16_t* out_bf16, float* out_f32, int64_t ld_out, float* out_lse, cudaStream_t s);

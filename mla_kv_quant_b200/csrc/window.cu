@@ -342,6 +342,7 @@ __global__ void __launch_bounds__(4 * D / 8) merge_splits_kernel(const DecodeArg
 // Window split (normal launch), then the INT2 kernel and the merge as programmatic
 // dependents.  Shapes and output alignment are checked by the caller.
 int launch_decode_tc(const DecodeArgs& a, int heads, cudaStream_t s, bool dependent);
+bool decode_tc_supported(const DecodeArgs& a, int heads);
 
 // Requests per window CTA (rpc): as many as shared memory and the per-thread staging
 // registers allow.
@@ -417,6 +418,25 @@ static int launch_window_first(const DecodeArgs& a, int win_ctas, int heads, uin
   if (rc != ROLAQ_OK) return rc;
   return d == 512 ? launch_merge_splits<512>(a, heads, out, out_sb, out_sh, out_lse, s)
                   : launch_merge_splits<256>(a, heads, out, out_sb, out_sh, out_lse, s);
+}
+
+// The split partials only (no merge): the window split first on the SMs a one-wave INT2 grid
+// leaves free, the INT2 kernel as its programmatic dependent; else the INT2 kernel and the
+// window split one after the other.
+int launch_decode(const DecodeArgs& a, int heads, cudaStream_t s);
+int launch_decode_partials(const DecodeArgs& a, int heads, cudaStream_t s) {
+  if (!decode_tc_supported(a, heads) || !window_first_fits(a)) return launch_decode(a, heads, s);
+  const int d = a.cache.latent_dim;
+  const int win_ctas = max(1, sm_count() - a.batch * a.num_splits);
+  int rc;
+  if (d == 512)
+    rc = heads == 16 ? launch_window_split<512, 64, 16>(a, win_ctas, s)
+                     : launch_window_split<512, 64, 8>(a, win_ctas, s);
+  else
+    rc = heads == 40 ? launch_window_split<256, 32, 40>(a, win_ctas, s)
+                     : launch_window_split<256, 32, 16>(a, win_ctas, s);
+  if (rc != ROLAQ_OK) return rc;
+  return launch_decode_tc(a, heads, s, true);
 }
 
 int launch_decode_windowed(const DecodeArgs& a, int heads, uint16_t* out, int64_t out_sb, int64_t out_sh,

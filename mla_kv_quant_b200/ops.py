@@ -243,17 +243,20 @@ def prepare_gf_splits(splits: torch.Tensor, quant: torch.Tensor, merge: torch.Te
 
 def packed_decode(q: torch.Tensor, view: LayerView, page_table: torch.Tensor, seq_lens: torch.Tensor,
                   sm_scale: float, num_splits: int, part_o: torch.Tensor, part_lse: torch.Tensor,
-                  out: torch.Tensor, out_lse: torch.Tensor | None = None, err: torch.Tensor | None = None,
+                  out: torch.Tensor | None, out_lse: torch.Tensor | None = None, err: torch.Tensor | None = None,
                   token_range: torch.Tensor | None = None) -> None:
-    """``rolaq_packed_decode``: q [B, H, D+Dr] bf16 -> out [B, H, D] bf16 (rotated frame)."""
+    """``rolaq_packed_decode``: q [B, H, D+Dr] bf16 -> out [B, H, D] bf16 (rotated frame).
+    ``out=None`` writes only the split partials (``part_o``, ``part_lse``; the window split's
+    at index ``num_splits``) for a caller that merges them itself."""
     _check(q, "q", torch.bfloat16, 3)
-    _check(out, "out", torch.bfloat16, 3)
+    if out is not None:
+        _check(out, "out", torch.bfloat16, 3)
     _check(page_table, "page_table", torch.int32, 2)
     _check(seq_lens, "seq_lens", torch.int32, 1)
     b, h, w = q.shape
     if w != view.latent_dim + view.rope_dim or q.stride(2) != 1:
         raise ValueError("q must be [B, H, D + Dr] with contiguous rows")
-    if tuple(out.shape) != (b, h, view.latent_dim) or out.stride(2) != 1:
+    if out is not None and (tuple(out.shape) != (b, h, view.latent_dim) or out.stride(2) != 1):
         raise ValueError("out must be [B, H, D] with contiguous rows")
     if page_table.shape[0] < b or page_table.stride(1) != 1 or seq_lens.numel() < b:
         raise ValueError("page_table / seq_lens too small")
@@ -271,8 +274,9 @@ def packed_decode(q: torch.Tensor, view: LayerView, page_table: torch.Tensor, se
     cs = view.c_struct()
     _lib.call("rolaq_packed_decode", q.data_ptr(), q.stride(0), q.stride(1), b, h, ctypes.byref(cs),
               page_table.data_ptr(), page_table.stride(0), page_table.shape[1], seq_lens.data_ptr(),
-              _lib.ptr(token_range), float(sm_scale), int(num_splits), part_o.data_ptr(), part_lse.data_ptr(), out.data_ptr(),
-              out.stride(0), out.stride(1), _lib.ptr(out_lse), _err_ptr(err), _lib.stream_ptr())
+              _lib.ptr(token_range), float(sm_scale), int(num_splits), part_o.data_ptr(), part_lse.data_ptr(),
+              _lib.ptr(out), out.stride(0) if out is not None else 0, out.stride(1) if out is not None else 0,
+              _lib.ptr(out_lse), _err_ptr(err), _lib.stream_ptr())
 
 
 def merge_partials(part_o: torch.Tensor, part_lse: torch.Tensor, out_bf16: torch.Tensor | None = None,

@@ -63,11 +63,14 @@ def gather_merge(o_local: torch.Tensor, lse_local: torch.Tensor, group=None,
 class SequenceSplitDecoder:
     """Decode attention for requests whose pages are spread over the ranks of ``group``."""
 
-    def __init__(self, pool, group=None):
+    def __init__(self, pool, group=None, exchange: "PeerExchange | None" = None):
+        """``exchange``: a :class:`PeerExchange` of the same group moves the partials over NVLink
+        peer memory; without one they go through one NCCL all-gather."""
         self.pool = pool
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        self.exchange = exchange
 
     def local_partial(self, q, layer_id, page_table, seq_lens, sm_scale, num_splits, token_range):
         """This rank's slice: its split partials LSE-merged in FP32, ``(o [B*H, D], lse [B*H])``.
@@ -92,6 +95,97 @@ class SequenceSplitDecoder:
         b, h, _ = q.shape
         rng = torch.tensor([rank_token_range(int(L), self.world, self.rank) for L in seq_lens_host],
                            dtype=torch.int32, device=q.device)
+        if self.exchange is not None:
+            d = self.pool.kv_lora_rank
+            part_o = torch.empty(b, h, num_splits + 1, d, dtype=torch.float32, device=q.device)
+            part_lse = torch.empty(b, h, num_splits + 1, dtype=torch.float32, device=q.device)
+            ops.packed_decode(q, self.pool.layer_view(layer_id), page_table, seq_lens, sm_scale, num_splits, part_o,
+                              part_lse, None, token_range=rng)  # the partials only: the push merges them
+            out = torch.empty(b, h, d, dtype=torch.bfloat16, device=q.device)
+            self.exchange.exchange(part_o, part_lse, out_bf16=out)
+            return out
         o, lse = self.local_partial(q, layer_id, page_table, seq_lens, sm_scale, num_splits, rng)
         out, _ = gather_merge(o, lse, self.group)
         return out.view(b, h, -1).to(torch.bfloat16)
+
+
+class PeerExchange:
+    """The sequence-split exchange over NVLink peer memory (``rolaq_peer_merge_push`` /
+    ``rolaq_peer_wait_merge``), in place of the NCCL all-gather of :func:`gather_merge`.
+
+    Every rank owns one receive buffer (``rolaq_device_alloc``) mapped into every other rank
+    with CUDA IPC; the kernel that merges a rank's splits writes the rank's FP32 partial
+    straight into all of them and flags it, and the final merge waits (bounded) for every
+    rank's flag.  Construction is collective (one ``all_gather_object`` of the IPC handles and
+    a barrier); :meth:`close` is collective too.  ``rows`` bounds ``batch * heads``."""
+
+    def __init__(self, rows: int, latent_dim: int, group=None, device: torch.device | None = None):
+        import ctypes
+
+        from . import _lib
+
+        self.group = group
+        self._dist = dist.is_available() and dist.is_initialized()  # a single rank needs no process group
+        self.world = dist.get_world_size(group) if self._dist else 1
+        self.rank = dist.get_rank(group) if self._dist else 0
+        self.rows, self.d = rows, latent_dim
+        dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        lib = _lib.load()
+        nbytes = lib.rolaq_peer_recv_bytes(self.world, rows, latent_dim)
+        if nbytes <= 0:
+            raise ValueError(f"no exchange for latent_dim {latent_dim}, rows {rows}")
+        own = ctypes.c_void_p()
+        _lib.call("rolaq_device_alloc", nbytes, ctypes.byref(own))
+        self._own = own.value
+        handle = (ctypes.c_char * _lib.IPC_HANDLE_BYTES)()
+        _lib.call("rolaq_ipc_get_handle", self._own, handle)
+        handles: list = [bytes(handle)]
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+        self._opened, ptrs = [], []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(self._own)
+                continue
+            p = ctypes.c_void_p()
+            _lib.call("rolaq_ipc_open", (ctypes.c_char * _lib.IPC_HANDLE_BYTES).from_buffer_copy(h), ctypes.byref(p))
+            self._opened.append(p.value)
+            ptrs.append(p.value)
+        self.peers = torch.tensor(ptrs, dtype=torch.int64, device=dev)  # addresses as seen by this process
+        self.state = torch.zeros(2, dtype=torch.int32, device=dev)
+        if self.world > 1:
+            dist.barrier(group)  # every rank holds every mapping before any push
+
+    def exchange(self, part_o: torch.Tensor, part_lse: torch.Tensor, out_bf16: torch.Tensor | None = None,
+                 out_f32: torch.Tensor | None = None, out_lse: torch.Tensor | None = None,
+                 err: torch.Tensor | None = None) -> None:
+        """``part_o [B, H, parts, D]`` / ``part_lse [B, H, parts]`` (a token-range decode's
+        split partials, contiguous) -> the merged output of all ranks, ``[B, H, D]``."""
+        from . import _lib
+
+        b, h, parts, d = part_o.shape
+        rows = b * h
+        if d != self.d or rows > self.rows or not part_o.is_contiguous() or not part_lse.is_contiguous():
+            raise ValueError("partials must be contiguous [B, H, parts, D] with B * H <= rows")
+        _lib.call("rolaq_peer_merge_push", part_o.data_ptr(), part_lse.data_ptr(), parts, rows, d,
+                  self.peers.data_ptr(), self.world, self.rank, self.state.data_ptr(), _lib.stream_ptr())
+        _lib.call("rolaq_peer_wait_merge", self._own, self.world, rows, d, self.state.data_ptr(),
+                  _lib.ptr(out_bf16), _lib.ptr(out_f32), _lib.ptr(out_lse), _lib.ptr(err), _lib.stream_ptr())
+
+    def close(self) -> None:
+        """Collective: unmap the peers' buffers and free this rank's, once no rank writes."""
+        from . import _lib
+
+        if self._own is None:
+            return
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier(self.group)
+        for p in self._opened:
+            _lib.call("rolaq_ipc_close", p)
+        self._opened = []
+        if self.world > 1:
+            dist.barrier(self.group)
+        _lib.call("rolaq_device_free", self._own)
+        self._own = None

@@ -1,0 +1,92 @@
+"""The sequence-split exchange over peer memory (``PeerExchange``): on one GPU the rank
+exchanges with itself (the same kernels, its own receive buffer as the only peer), and the
+result must equal the local LSE merge of the same split partials; with two or more GPUs the
+bench's ``--mode seqsplit`` compares it with the NCCL all-gather path."""
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_helpers import GpuPool, bits, fill_requests
+from mla_kv_quant_b200 import ops, synth
+from mla_kv_quant_b200.seqsplit import PeerExchange
+from oracle import decode as odecode
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("d,dr,h", [(512, 64, 16), (256, 32, 40)])
+def test_peer_exchange_single_rank_equals_local_merge(d, dr, h):
+    seq_lens = [900, 257, 64]
+    b = len(seq_lens)
+    g = torch.Generator().manual_seed(81)
+    pages = 15
+    pt = (torch.randperm(b * pages, generator=g) + 1).to(torch.int32).reshape(b, pages).cuda()
+    pool = GpuPool(64 * (b * pages + 1), d, dr, max_reqs=b, sink=4, recent=16)
+    fill_requests(pool, seq_lens, pt, synth.rotation(d, seed=82), ops.codec_serving(0.85, synth.signal_gain(0.85)),
+                  seed=83)
+    q = synth.normal_bf16((b, h, d + dr), seed=84, device="cuda")
+    sl = torch.tensor(seq_lens, dtype=torch.int32, device="cuda")
+    sm = 0.07
+    parts = 4
+    part_o = torch.empty(b, h, parts, d, device="cuda")
+    part_lse = torch.empty(b, h, parts, device="cuda")
+    scratch = torch.empty(b, h, d, dtype=torch.bfloat16, device="cuda")
+    ops.packed_decode(q, pool.view(), pt, sl, sm, parts - 1, part_o, part_lse, scratch)
+    ref32 = torch.empty(b * h, d, device="cuda")
+    ref_lse = torch.empty(b * h, device="cuda")
+    ops.merge_partials(part_o.view(b * h, parts, d).transpose(0, 1), part_lse.view(b * h, parts).t(), out_f32=ref32,
+                       out_lse=ref_lse)
+    xch = PeerExchange(b * h, d)
+    try:
+        err = torch.zeros(1, dtype=torch.int32, device="cuda")
+        for step in range(3):  # both parities of the receive buffer, and a reused state
+            out = torch.full((b, h, d), float("nan"), dtype=torch.bfloat16, device="cuda")
+            out32 = torch.full((b, h, d), float("nan"), device="cuda")
+            lse = torch.full((b * h,), float("nan"), device="cuda")
+            xch.exchange(part_o, part_lse, out_bf16=out, out_f32=out32, out_lse=lse, err=err)
+            torch.cuda.synchronize()
+            assert int(err.item()) == 0
+            assert int(xch.state[0].item()) == step + 1
+            # one partial per rank: the merge of a single partial is the partial itself
+            assert torch.allclose(out32.view(b * h, d), ref32, rtol=1e-6, atol=1e-6), step
+            assert torch.allclose(lse, ref_lse, rtol=1e-6, atol=1e-6)
+            assert torch.equal(out, out32.to(torch.bfloat16))  # the BF16 output is the FP32 result rounded
+    finally:
+        xch.close()
+    # and the merged result is the decode the oracle computes
+    ref, _ = odecode.decode(pool.to_oracle(), bits(q), pt.cpu().numpy(), seq_lens, sm)
+    assert np.abs(ref32.view(b, h, d).cpu().numpy() - ref).max() <= 2e-2
+
+
+def test_partials_only_decode_matches_merged_call():
+    """``packed_decode(out=None)`` writes the same split partials the merged call merges: the
+    exchange of those partials (one rank) equals the merged call's output."""
+    d, dr, h = 512, 64, 16
+    seq_lens = [1300, 90]
+    b = len(seq_lens)
+    g = torch.Generator().manual_seed(91)
+    pages = 21
+    pt = (torch.randperm(b * pages, generator=g) + 1).to(torch.int32).reshape(b, pages).cuda()
+    pool = GpuPool(64 * (b * pages + 1), d, dr, max_reqs=b, sink=4, recent=16)
+    fill_requests(pool, seq_lens, pt, synth.rotation(d, seed=92), ops.codec_serving(0.85, synth.signal_gain(0.85)),
+                  seed=93)
+    q = synth.normal_bf16((b, h, d + dr), seed=94, device="cuda")
+    sl = torch.tensor(seq_lens, dtype=torch.int32, device="cuda")
+    parts = 3
+    merged = torch.empty(b, h, d, dtype=torch.bfloat16, device="cuda")
+    ops.packed_decode(q, pool.view(), pt, sl, 0.07, parts - 1, torch.empty(b, h, parts, d, device="cuda"),
+                      torch.empty(b, h, parts, device="cuda"), merged)
+    part_o = torch.full((b, h, parts, d), float("nan"), device="cuda")
+    part_lse = torch.full((b, h, parts), float("nan"), device="cuda")
+    ops.packed_decode(q, pool.view(), pt, sl, 0.07, parts - 1, part_o, part_lse, None)
+    xch = PeerExchange(b * h, d)
+    try:
+        out = torch.empty(b, h, d, dtype=torch.bfloat16, device="cuda")
+        xch.exchange(part_o, part_lse, out_bf16=out)
+        torch.cuda.synchronize()
+    finally:
+        xch.close()
+    assert torch.isfinite(part_lse).all() or (part_lse == float("-inf")).any()
+    diff = (out.float() - merged.float()).abs()
+    assert float(diff.max()) <= 2 ** -8 * float(merged.float().abs().max()), float(diff.max())
