@@ -90,3 +90,27 @@ def test_partials_only_decode_matches_merged_call():
     assert torch.isfinite(part_lse).all() or (part_lse == float("-inf")).any()
     diff = (out.float() - merged.float()).abs()
     assert float(diff.max()) <= 2 ** -8 * float(merged.float().abs().max()), float(diff.max())
+
+
+def test_peer_wait_gives_up_when_no_rank_pushes():
+    """A rank whose peers never push: the merge's wait ends after its bound (~2 s) with
+    ROLAQ_DEV_PEER_TIMEOUT in err and a zero output, and the context stays usable.  The
+    missing push is made on the host: the step counter is moved past every flag."""
+    from mla_kv_quant_b200 import _lib
+
+    d, rows = 512, 8
+    xch = PeerExchange(rows, d)
+    try:
+        xch.state[0] = 5  # a step no rank has flagged
+        out = torch.full((rows, d), float("nan"), dtype=torch.bfloat16, device="cuda")
+        err = torch.zeros(1, dtype=torch.int32, device="cuda")
+        _lib.call("rolaq_peer_wait_merge", xch._own, xch.world, rows, d, xch.state.data_ptr(), out.data_ptr(), None,
+                  None, err.data_ptr(), _lib.stream_ptr())
+        torch.cuda.synchronize()
+        assert int(err.item()) & _lib.DEV_PEER_TIMEOUT
+        assert torch.equal(out.float(), torch.zeros(rows, d, device="cuda"))
+        # the device still answers
+        assert float(torch.ones(4, device="cuda").sum().item()) == 4.0
+    finally:
+        xch.state[0] = 0
+        xch.close()
