@@ -699,7 +699,6 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int w = 0; w < HS / 2; ++w) *reinterpret_cast<uint32_t*>(prow + sw128(t, 2 * HS * k + 4 * w)) = pw[w];
         }
       }
-      fence_proxy_async();
       // -- 4. the PV-A tile of i+1 into buffer (i+1) & 1, last read by PV(i-1).  PV(i-1) is
       //       waited for on every tile (the last one too): PREADY(i) then cannot complete
       //       before the MMA warp has taken PREADY(i-1), so its parity wait never aliases. --
@@ -720,7 +719,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       } else if (alive && i >= 1) {
         alive = mbar_wait(&bars[B_PV], (i - 1) & 1, a.err);
       }
-      fence_proxy_async();
+      fence_proxy_async();  // the P' and PV-A stores above, for the tensor core's reads
       mbar_arrive(&bars[B_PREADY]);  // P'(i), the PV-A tile of i+1 and a rescaled O are ready;
                                      // params stage i & 1 has been read
     }
