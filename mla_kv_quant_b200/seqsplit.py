@@ -168,6 +168,17 @@ class PeerExchange:
         rows = b * h
         if d != self.d or rows > self.rows or not part_o.is_contiguous() or not part_lse.is_contiguous():
             raise ValueError("partials must be contiguous [B, H, parts, D] with B * H <= rows")
+        if part_o.dtype != torch.float32 or part_lse.dtype != torch.float32 or tuple(part_lse.shape) != (b, h, parts):
+            raise ValueError("part_o / part_lse must be float32 [B, H, parts, D] / [B, H, parts]")
+        dev = self.peers.device
+        for name, t, dt, n in (("part_o", part_o, None, None), ("out_bf16", out_bf16, torch.bfloat16, rows * d),
+                               ("out_f32", out_f32, torch.float32, rows * d), ("out_lse", out_lse, torch.float32, rows)):
+            if t is None:
+                continue
+            if t.device != dev:
+                raise ValueError(f"{name} must be on {dev}")
+            if dt is not None and (t.dtype != dt or t.numel() != n or not t.is_contiguous()):
+                raise ValueError(f"{name} must be contiguous {dt} with {n} elements")
         _lib.call("rolaq_peer_merge_push", part_o.data_ptr(), part_lse.data_ptr(), parts, rows, d,
                   self.peers.data_ptr(), self.world, self.rank, self.state.data_ptr(), _lib.stream_ptr())
         _lib.call("rolaq_peer_wait_merge", self._own, self.world, rows, d, self.state.data_ptr(),
