@@ -992,7 +992,16 @@ def run_seqsplit(args, rank, world, dev):
         torch.cuda.synchronize()
         if it >= args.warmup:
             gl.append(ev[0].elapsed_time(ev[2]) * 1e3)
+    reps = 50
+    if world > 1:
+        torch.distributed.barrier()
     torch.cuda.synchronize()
+    ev[0].record()
+    for _ in range(reps):
+        graph.replay()
+    ev[2].record()
+    torch.cuda.synchronize()
+    gs_us = ev[0].elapsed_time(ev[2]) * 1e3 / reps
     del graph  # before the process group goes: the graph holds the NCCL call
     g_us = sorted(gl)[len(gl) // 2]
 
@@ -1045,18 +1054,33 @@ def run_seqsplit(args, rank, world, dev):
         torch.cuda.synchronize()
         if it >= args.warmup:
             pg.append(ev[0].elapsed_time(ev[2]) * 1e3)
+    # steady state: the graph replayed back to back, as consecutive decode steps run; the
+    # exchange itself keeps the ranks in step (no host barrier between replays)
+    reps = 50
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    ev[0].record()
+    for _ in range(reps):
+        graph.replay()
+    ev[2].record()
+    torch.cuda.synchronize()
+    ps_us = ev[0].elapsed_time(ev[2]) * 1e3 / reps
     del graph
     peer_err = int(perr.item())
     xch.close()
     p_us, pg_us = sorted(pl)[len(pl) // 2], sorted(pg)[len(pg) // 2]
 
-    t = torch.tensor([k_us, c_us, k_us + c_us, g_us, p_us, pg_us, peer_diff, float(peer_err)], device=dev)
+    t = torch.tensor([k_us, c_us, k_us + c_us, g_us, p_us, pg_us, peer_diff, float(peer_err), ps_us, gs_us],
+                     device=dev)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     return {"mode": "seqsplit", "n_gpus": world, "batch": 1, "ctx": ctx, "tokens_per_rank": n,
             "num_splits_per_rank": splits, "us_per_layer": float(t[2]), "kernel_us": float(t[0]),
             "gather_merge_us": float(t[1]), "us_per_layer_graph": float(t[3]),
+            "us_per_layer_graph_steady": float(t[9]),
             "peer": {"us_per_layer": float(t[4]), "us_per_layer_graph": float(t[5]),
+                     "us_per_layer_graph_steady": float(t[8]),
                      "max_abs_diff_vs_nccl": float(t[6]), "err_bits": int(t[7]),
                      "path": "the slice's split partials (window split + INT2 kernel, no merge) + one kernel that "
                              "merges them and writes the FP32 partial into every rank's receive buffer over "
@@ -1065,7 +1089,8 @@ def run_seqsplit(args, rank, world, dev):
             "note": "median over steps of each rank, max over ranks; kernel = the slice's decode call (INT2 "
                     "splits + window + merge) and its FP32 partial merge, gather_merge = one NCCL "
                     "all-gather of the (o, lse) partials + the merge kernel (eager launches); "
-                    "us_per_layer_graph = the same layer replayed from a CUDA graph"}
+                    "us_per_layer_graph = the same layer replayed from a CUDA graph after a host barrier "
+                    "(includes the ranks' start skew); *_steady = 50 replays back to back / 50"}
 
 
 def main():

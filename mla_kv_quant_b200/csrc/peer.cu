@@ -98,6 +98,10 @@ __global__ void __launch_bounds__(kRowsPerCta * D / 8) merge_push_kernel(const f
   const int row = blockIdx.x * kRowsPerCta + threadIdx.x / TPR;
   const int j = 8 * (threadIdx.x % TPR), lane = threadIdx.x & 31;
   const int64_t slot = int64_t(rows) * (D + 4);
+  // launched as a programmatic dependent of the decode kernel: its partials (and, through it,
+  // the window split's) are complete once this returns
+  grid_dependency_wait();
+  if (threadIdx.x == 0) grid_launch_dependents();  // the wait kernel may take its SMs now
   const int32_t step = state[0] + 1;  // this exchange; state[0] moves only when the whole grid is done
   if (row < rows) {
     float acc[8];
@@ -136,7 +140,8 @@ __global__ void __launch_bounds__(kRowsPerCta * D / 8) wait_merge_kernel(const f
   constexpr int TPR = D / 8;
   __shared__ int ok_all;
   const int64_t slot = int64_t(rows) * (D + 4);
-  const int32_t step = state[0];  // written by this rank's push (earlier on the stream)
+  grid_dependency_wait();  // a programmatic dependent of this rank's push: state[0] is its step
+  const int32_t step = state[0];
   if (threadIdx.x == 0) {
     const int32_t* flags = reinterpret_cast<const int32_t*>(recv + 2 * world * slot);
     bool ok = true;
@@ -188,28 +193,42 @@ int64_t peer_recv_bytes(int world, int64_t rows, int d) {
   return (2 * int64_t(world) * rows * (d + 4)) * 4 + ((int64_t(world) * 4 + 15) / 16) * 16;
 }
 
+// Both kernels are launched as programmatic dependents of the kernel before them in the stream
+// (the decode kernel, then the push): their CTAs are placed while that grid runs and wait for
+// its completion (griddepcontrol.wait) before reading what it wrote.
+template <typename... KArgs, typename... Args>
+static int launch_dependent(void (*kernel)(KArgs...), int ctas, int threads, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(ctas));
+  cfg.blockDim = dim3(static_cast<unsigned>(threads));
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kernel, args...) != cudaSuccess) return ROLAQ_ECUDA;
+  return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;
+}
+
 int launch_peer_merge_push(const float* part_o, const float* part_lse, int n_parts, int rows, int d,
                            const uint64_t* peers, int world, int rank, int32_t* state, cudaStream_t s) {
   const int ctas = (rows + peer::kRowsPerCta - 1) / peer::kRowsPerCta;
   if (d == 512)
-    peer::merge_push_kernel<512><<<ctas, peer::kRowsPerCta * 64, 0, s>>>(part_o, part_lse, n_parts, rows, peers, world,
-                                                                         rank, state);
-  else
-    peer::merge_push_kernel<256><<<ctas, peer::kRowsPerCta * 32, 0, s>>>(part_o, part_lse, n_parts, rows, peers, world,
-                                                                         rank, state);
-  return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;
+    return launch_dependent(peer::merge_push_kernel<512>, ctas, peer::kRowsPerCta * 64, s, part_o, part_lse, n_parts,
+                            rows, peers, world, rank, state);
+  return launch_dependent(peer::merge_push_kernel<256>, ctas, peer::kRowsPerCta * 32, s, part_o, part_lse, n_parts,
+                          rows, peers, world, rank, state);
 }
 
 int launch_peer_wait_merge(const float* recv, int world, int rows, int d, const int32_t* state, uint16_t* out_bf16,
                            float* out_f32, float* out_lse, int32_t* err, cudaStream_t s) {
   const int ctas = (rows + peer::kRowsPerCta - 1) / peer::kRowsPerCta;
   if (d == 512)
-    peer::wait_merge_kernel<512><<<ctas, peer::kRowsPerCta * 64, 0, s>>>(recv, world, rows, state, out_bf16, out_f32,
-                                                                         out_lse, err);
-  else
-    peer::wait_merge_kernel<256><<<ctas, peer::kRowsPerCta * 32, 0, s>>>(recv, world, rows, state, out_bf16, out_f32,
-                                                                         out_lse, err);
-  return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;
+    return launch_dependent(peer::wait_merge_kernel<512>, ctas, peer::kRowsPerCta * 64, s, recv, world, rows, state,
+                            out_bf16, out_f32, out_lse, err);
+  return launch_dependent(peer::wait_merge_kernel<256>, ctas, peer::kRowsPerCta * 32, s, recv, world, rows, state,
+                          out_bf16, out_f32, out_lse, err);
 }
 
 }  // namespace rolaq
