@@ -936,13 +936,12 @@ def run_seqsplit(args, rank, world, dev):
     parts = splits + 1
     part_o = torch.empty(1, HEADS, parts, D, device=dev)
     part_lse = torch.empty(1, HEADS, parts, device=dev)
-    scratch = torch.empty(1, HEADS, D, dtype=torch.bfloat16, device=dev)
     lse_loc = torch.empty(HEADS, device=dev)
     o_loc = torch.empty(HEADS, D, device=dev)
     sm = 1.0 / math.sqrt(192.0)
 
     def layer():  # the slice's FP32 partial and LSE, as SequenceSplitDecoder.local_partial
-        ops.packed_decode(q, view, pt, sl, sm, splits, part_o, part_lse, scratch, token_range=rng)
+        ops.packed_decode(q, view, pt, sl, sm, splits, part_o, part_lse, None, token_range=rng)
         ops.merge_partials(part_o.view(HEADS, parts, D).transpose(0, 1), part_lse.view(HEADS, parts).t(),
                            out_f32=o_loc, out_lse=lse_loc)
 
@@ -1086,8 +1085,8 @@ def run_seqsplit(args, rank, world, dev):
                              "merges them and writes the FP32 partial into every rank's receive buffer over "
                              "NVLink (CUDA IPC) + a merge that waits for every rank's partial; no library "
                              "collective"},
-            "note": "median over steps of each rank, max over ranks; kernel = the slice's decode call (INT2 "
-                    "splits + window + merge) and its FP32 partial merge, gather_merge = one NCCL "
+            "note": "median over steps of each rank, max over ranks; kernel = the slice's split partials (INT2 "
+                    "splits + window) and their FP32 merge, gather_merge = one NCCL "
                     "all-gather of the (o, lse) partials + the merge kernel (eager launches); "
                     "us_per_layer_graph = the same layer replayed from a CUDA graph after a host barrier "
                     "(includes the ranks' start skew); *_steady = 50 replays back to back / 50"}

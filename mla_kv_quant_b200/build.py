@@ -22,7 +22,7 @@ CSRC = PKG / "csrc"
 OUT_DIR = PKG / "_lib"
 LIB = OUT_DIR / "librolaq_b200.so"
 SOURCES = ["abi.cu", "writer.cu", "codec.cu", "decode.cu", "decode_tc.cu", "proj.cu", "window.cu", "peer.cu"]
-HEADERS = ["common.cuh", "kernels.cuh"]
+HEADERS = ["common.cuh", "kernels.cuh", "merge.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

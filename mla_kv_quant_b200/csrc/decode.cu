@@ -20,6 +20,7 @@
 // The window split reads the BF16 ring rows (or the INT2 codes when a ring row no
 // longer belongs to the slot) in FP32 on the CUDA cores.
 #include "kernels.cuh"
+#include "merge.cuh"
 
 namespace rolaq {
 
@@ -810,6 +811,29 @@ __global__ void merge_kernel(const float* __restrict__ part_o, int64_t row_strid
   if (threadIdx.x == 0 && out_lse) out_lse[row] = den > 0.f ? mref + logf(den) : -INFINITY;
 }
 
+// Many partials (n_parts >= wide::kMinParts): a CTA per (row, 128-column chunk), its warps
+// taking the partials in turn; rows, parts and outputs as merge_kernel<true> reads them.
+__global__ void __launch_bounds__(wide::kThreads)
+    merge_wide_kernel(const float* __restrict__ part_o, int64_t row_stride, int64_t part_stride,
+                      const float* __restrict__ part_lse, int64_t lse_row_stride, int64_t lse_part_stride, int n_parts,
+                      int d, uint16_t* __restrict__ out_bf16, float* __restrict__ out_f32, int64_t ld_out,
+                      float* __restrict__ out_lse) {
+  __shared__ float4 red[wide::kWarps][32];
+  const int chunks = (d + wide::kCols - 1) / wide::kCols;
+  const int64_t row = blockIdx.x / chunks;
+  const int c0 = static_cast<int>(blockIdx.x % chunks) * wide::kCols;
+  float4 res;
+  const float lse = wide::merge_chunk(part_o + row * row_stride, part_stride, part_lse + row * lse_row_stride,
+                                      lse_part_stride, n_parts, c0, d, red, res);
+  if (threadIdx.x >= 32) return;
+  const int col = c0 + 4 * threadIdx.x;
+  if (col < d) {
+    if (out_f32) *reinterpret_cast<float4*>(out_f32 + row * ld_out + col) = res;
+    if (out_bf16) *reinterpret_cast<uint2*>(out_bf16 + row * ld_out + col) = wide::to_bf16x4(res);
+  }
+  if (c0 == 0 && threadIdx.x == 0 && out_lse) out_lse[row] = lse;
+}
+
 // Window split + LSE merge for the tcgen05 path, one CTA per (request, 4 heads), 256 threads.
 //
 // Phase 1 does not read the INT2 partials, so it runs while the tcgen05 kernel drains (this
@@ -1198,6 +1222,13 @@ int launch_merge(const float* part_o, int64_t row_stride, int64_t part_stride, c
   const bool vec = d % 4 == 0 && row_stride % 4 == 0 && part_stride % 4 == 0 && a16(part_o) &&
                    (out_f32 == nullptr || (a16(out_f32) && ld_out % 4 == 0)) &&
                    (out_bf16 == nullptr || ((reinterpret_cast<uintptr_t>(out_bf16) & 7u) == 0 && ld_out % 4 == 0));
+  const int64_t wide_ctas = rows * ((d + wide::kCols - 1) / wide::kCols);
+  if (vec && n_parts >= wide::kMinParts && wide_ctas <= 0x7FFFFFFF) {
+    merge_wide_kernel<<<static_cast<unsigned>(wide_ctas), wide::kThreads, 0, s>>>(
+        part_o, row_stride, part_stride, part_lse, lse_row_stride, lse_part_stride, n_parts, d, out_bf16, out_f32,
+        ld_out, out_lse);
+    return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;
+  }
   const int threads = d >= 512 ? 128 : 64;
   const size_t smem = size_t(n_parts) * sizeof(float);
   if (smem > 48 * 1024) return ROLAQ_EUNSUPPORTED;

@@ -19,6 +19,7 @@
 // Double buffering by step parity suffices: a rank pushes step s + 2 only after its wait for
 // step s + 1, which needs every rank's push of step s + 1, issued after that rank's merge of s.
 #include "kernels.cuh"
+#include "merge.cuh"
 
 namespace rolaq {
 namespace peer {
@@ -88,38 +89,59 @@ __device__ __forceinline__ float merge_row(const float* o, int64_t o_stride, con
   return den > 0.f ? mref + logf(den) : -INFINITY;
 }
 
-template <int D>
-__global__ void __launch_bounds__(kRowsPerCta * D / 8) merge_push_kernel(const float* __restrict__ part_o,
-                                                                         const float* __restrict__ part_lse,
-                                                                         int n_parts, int rows,
-                                                                         const uint64_t* __restrict__ peers,
-                                                                         int world, int rank, int32_t* state) {
+// WIDE (many partials): a CTA per (row, 128-column chunk), its warps taking the partials in
+// turn (wide::merge_chunk); else kRowsPerCta rows per CTA, D / 8 threads per row.
+template <int D, bool WIDE>
+__global__ void __launch_bounds__(WIDE ? wide::kThreads : kRowsPerCta * D / 8)
+    merge_push_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse, int n_parts, int rows,
+                      const uint64_t* __restrict__ peers, int world, int rank, int32_t* state) {
   constexpr int TPR = D / 8;  // threads per row
-  const int row = blockIdx.x * kRowsPerCta + threadIdx.x / TPR;
-  const int j = 8 * (threadIdx.x % TPR), lane = threadIdx.x & 31;
   const int64_t slot = int64_t(rows) * (D + 4);
   // launched as a programmatic dependent of the decode kernel: its partials (and, through it,
   // the window split's) are complete once this returns
   grid_dependency_wait();
   if (threadIdx.x == 0) grid_launch_dependents();  // the wait kernel may take its SMs now
   const int32_t step = state[0] + 1;  // this exchange; state[0] moves only when the whole grid is done
-  if (row < rows) {
-    float acc[8];
-    const float lse = merge_row(part_o + int64_t(row) * n_parts * D + j, D, part_lse + int64_t(row) * n_parts, 1,
-                                n_parts, lane, acc);
-    const int64_t off = (int64_t(step & 1) * world + rank) * slot + int64_t(row) * (D + 4);
-    for (int q = 0; q < world; ++q) {  // NVLink stores into every rank's receive buffer
-      float* dst = reinterpret_cast<float*>(peers[q]) + off;
-      reinterpret_cast<float4*>(dst + j)[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      reinterpret_cast<float4*>(dst + j)[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
-      if (j == 0) dst[D] = lse;
+  if (WIDE) {
+    __shared__ float4 red[wide::kWarps][32];
+    constexpr int CH = D / wide::kCols;
+    const int row = blockIdx.x / CH, c0 = (blockIdx.x % CH) * wide::kCols;
+    float4 res;
+    const float lse = wide::merge_chunk(part_o + int64_t(row) * n_parts * D, D, part_lse + int64_t(row) * n_parts, 1,
+                                        n_parts, c0, D, red, res);
+    if (threadIdx.x < 32) {
+      const int64_t off = (int64_t(step & 1) * world + rank) * slot + int64_t(row) * (D + 4);
+      for (int q = 0; q < world; ++q) {  // NVLink stores into every rank's receive buffer
+        float* dst = reinterpret_cast<float*>(peers[q]) + off;
+        reinterpret_cast<float4*>(dst + c0)[threadIdx.x] = res;
+        if (c0 == 0 && threadIdx.x == 0) dst[D] = lse;
+      }
+    }
+  } else {
+    const int row = blockIdx.x * kRowsPerCta + threadIdx.x / TPR;
+    const int j = 8 * (threadIdx.x % TPR), lane = threadIdx.x & 31;
+    if (row < rows) {
+      float acc[8];
+      const float lse = merge_row(part_o + int64_t(row) * n_parts * D + j, D, part_lse + int64_t(row) * n_parts, 1,
+                                  n_parts, lane, acc);
+      const int64_t off = (int64_t(step & 1) * world + rank) * slot + int64_t(row) * (D + 4);
+      for (int q = 0; q < world; ++q) {  // NVLink stores into every rank's receive buffer
+        float* dst = reinterpret_cast<float*>(peers[q]) + off;
+        reinterpret_cast<float4*>(dst + j)[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        reinterpret_cast<float4*>(dst + j)[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        if (j == 0) dst[D] = lse;
+      }
     }
   }
-  __threadfence_system();  // this thread's stores reach every peer before the CTA reports
+  // The CTA's stores are ordered before its count by the barrier and a GPU-scope fence (every
+  // CTA of the grid is on this GPU); the last CTA to count acquires them all and makes them
+  // visible system-wide with one fence before it releases the flags.  Release and acquire
+  // are cumulative, so a peer that acquires a flag sees every CTA's stores.
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence();
     const int done = atomicAdd(&state[1], 1);
-    if (done == gridDim.x - 1) {  // the grid's last CTA: every CTA's stores are visible system-wide
+    if (done == gridDim.x - 1) {  // the grid's last CTA
       __threadfence_system();
       for (int q = 0; q < world; ++q) {
         int32_t* flags = reinterpret_cast<int32_t*>(reinterpret_cast<float*>(peers[q]) + 2 * world * slot);
@@ -213,12 +235,20 @@ static int launch_dependent(void (*kernel)(KArgs...), int ctas, int threads, cud
 
 int launch_peer_merge_push(const float* part_o, const float* part_lse, int n_parts, int rows, int d,
                            const uint64_t* peers, int world, int rank, int32_t* state, cudaStream_t s) {
+  if (n_parts >= wide::kMinParts) {  // same rule as launch_merge, so both exchanges merge alike
+    const int ctas = rows * (d / wide::kCols);
+    if (d == 512)
+      return launch_dependent(peer::merge_push_kernel<512, true>, ctas, wide::kThreads, s, part_o, part_lse, n_parts,
+                              rows, peers, world, rank, state);
+    return launch_dependent(peer::merge_push_kernel<256, true>, ctas, wide::kThreads, s, part_o, part_lse, n_parts,
+                            rows, peers, world, rank, state);
+  }
   const int ctas = (rows + peer::kRowsPerCta - 1) / peer::kRowsPerCta;
   if (d == 512)
-    return launch_dependent(peer::merge_push_kernel<512>, ctas, peer::kRowsPerCta * 64, s, part_o, part_lse, n_parts,
-                            rows, peers, world, rank, state);
-  return launch_dependent(peer::merge_push_kernel<256>, ctas, peer::kRowsPerCta * 32, s, part_o, part_lse, n_parts,
-                          rows, peers, world, rank, state);
+    return launch_dependent(peer::merge_push_kernel<512, false>, ctas, peer::kRowsPerCta * 64, s, part_o, part_lse,
+                            n_parts, rows, peers, world, rank, state);
+  return launch_dependent(peer::merge_push_kernel<256, false>, ctas, peer::kRowsPerCta * 32, s, part_o, part_lse,
+                          n_parts, rows, peers, world, rank, state);
 }
 
 int launch_peer_wait_merge(const float* recv, int world, int rows, int d, const int32_t* state, uint16_t* out_bf16,

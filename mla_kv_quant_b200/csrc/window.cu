@@ -19,6 +19,7 @@
 // INT2 grid's last CTAs retire and wait (griddepcontrol.wait) for that grid, which itself
 // waits for the window kernel before it exits.
 #include "kernels.cuh"
+#include "merge.cuh"
 
 namespace rolaq {
 namespace win {
@@ -337,6 +338,26 @@ __global__ void __launch_bounds__(4 * D / 8) merge_splits_kernel(const DecodeArg
   if (threadIdx.x % TPH == 0 && out_lse) out_lse[row] = den > 0.f ? mref + logf(den) : -INFINITY;
 }
 
+// The same merge for many splits (num_splits + 1 >= wide::kMinParts): a CTA per (request,
+// head, 128-column chunk), its warps taking the splits in turn.
+template <int D>
+__global__ void __launch_bounds__(wide::kThreads) merge_splits_wide_kernel(const DecodeArgs a, int heads,
+                                                                           uint16_t* __restrict__ out, int64_t out_sb,
+                                                                           int64_t out_sh, float* __restrict__ out_lse) {
+  __shared__ float4 red[wide::kWarps][32];
+  constexpr int CH = D / wide::kCols;
+  const int64_t row = blockIdx.x / CH;  // b * heads + h
+  const int c0 = (blockIdx.x % CH) * wide::kCols;
+  const int S = a.num_splits + 1;
+  grid_dependency_wait();  // the INT2 kernel (and through it the window kernel) has completed
+  float4 res;
+  const float lse = wide::merge_chunk(a.part_o + row * S * D, D, a.part_lse + row * S, 1, S, c0, D, red, res);
+  if (threadIdx.x >= 32) return;
+  const int64_t b = row / heads, h = row % heads;
+  reinterpret_cast<uint2*>(out + b * out_sb + h * out_sh + c0)[threadIdx.x] = wide::to_bf16x4(res);
+  if (c0 == 0 && threadIdx.x == 0 && out_lse) out_lse[row] = lse;
+}
+
 }  // namespace win
 
 // Window split (normal launch), then the INT2 kernel and the merge as programmatic
@@ -386,9 +407,11 @@ static int launch_window_split(const DecodeArgs& a, int max_ctas, cudaStream_t s
 template <int D>
 static int launch_merge_splits(const DecodeArgs& a, int heads, uint16_t* out, int64_t out_sb, int64_t out_sh,
                                float* out_lse, cudaStream_t s) {
+  const bool many = a.num_splits + 1 >= wide::kMinParts;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(int64_t(a.batch) * heads / 4));
-  cfg.blockDim = dim3(4 * D / 8);
+  cfg.gridDim = dim3(static_cast<unsigned>(many ? int64_t(a.batch) * heads * (D / wide::kCols)
+                                                : int64_t(a.batch) * heads / 4));
+  cfg.blockDim = dim3(many ? wide::kThreads : 4 * D / 8);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -396,8 +419,10 @@ static int launch_merge_splits(const DecodeArgs& a, int heads, uint16_t* out, in
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, win::merge_splits_kernel<D>, a, heads, out, out_sb, out_sh, out_lse) != cudaSuccess)
-    return ROLAQ_ECUDA;
+  const cudaError_t e =
+      many ? cudaLaunchKernelEx(&cfg, win::merge_splits_wide_kernel<D>, a, heads, out, out_sb, out_sh, out_lse)
+           : cudaLaunchKernelEx(&cfg, win::merge_splits_kernel<D>, a, heads, out, out_sb, out_sh, out_lse);
+  if (e != cudaSuccess) return ROLAQ_ECUDA;
   return cudaGetLastError() == cudaSuccess ? ROLAQ_OK : ROLAQ_ECUDA;
 }
 

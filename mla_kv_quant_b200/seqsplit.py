@@ -81,9 +81,8 @@ class SequenceSplitDecoder:
         parts = num_splits + 1
         part_o = torch.empty(b, h, parts, d, dtype=torch.float32, device=q.device)
         part_lse = torch.empty(b, h, parts, dtype=torch.float32, device=q.device)
-        scratch = torch.empty(b, h, d, dtype=torch.bfloat16, device=q.device)
         ops.packed_decode(q, self.pool.layer_view(layer_id), page_table, seq_lens, sm_scale, num_splits, part_o,
-                          part_lse, scratch, token_range=token_range)
+                          part_lse, None, token_range=token_range)  # the partials only: merged below in FP32
         o = torch.empty(b * h, d, dtype=torch.float32, device=q.device)
         lse = torch.empty(b * h, dtype=torch.float32, device=q.device)
         ops.merge_partials(part_o.view(b * h, parts, d).transpose(0, 1), part_lse.view(b * h, parts).t(), out_f32=o,
