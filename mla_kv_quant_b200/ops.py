@@ -292,24 +292,46 @@ def merge_partials(part_o: torch.Tensor, part_lse: torch.Tensor, out_bf16: torch
               _lib.ptr(out_lse), _lib.stream_ptr())
 
 
+def _window_rpc(latent_dim: int, rope_dim: int, window_rows: int) -> int:
+    """Requests one window CTA stages at a time (``window_rpc`` in ``csrc/window.cu``)."""
+    if window_rows <= 0:
+        return 8
+    per_req = window_rows * (latent_dim + rope_dim) * 4 + 2 * 32 * 8 + 4
+    rpc = min((200 * 1024) // per_req, (12 * 512) // (window_rows * (latent_dim + rope_dim) // 8))
+    return max(1, min(rpc, 8))
+
+
 def default_num_splits(batch: int, max_ctx: int, sm_count: int = 148, ctas_per_sm: int | None = None,
-                       latent_dim: int = 512, rope_dim: int = 64, heads: int = 16) -> int:
+                       latent_dim: int = 512, rope_dim: int = 64, heads: int = 16, window_rows: int = 20) -> int:
     """Pick the number of INT2 KV splits per request: the count that minimises
     ``waves * (tiles per split + 3)``, where a wave is ``sm_count * ctas_per_sm`` CTAs, a tile is
     128 tokens and the 3 is a CTA's fixed cost (set-up, query conversion, epilogue) in tiles,
-    fitted to split-count sweeps on B200 (B64 x 16K: 9 splits; B128 x 8K: 2-3).  Ties go to
-    fewer splits.  The tcgen05 kernel (every built shape) holds one CTA per SM."""
+    fitted to split-count sweeps on B200 (B64 x 16K: 2 splits; B128 x 8K: 1).  Ties go to
+    fewer splits.  The tcgen05 kernel (every built shape) holds one CTA per SM.
+
+    A one-wave grid of 15 or more splits that leaves too few SMs for the window split to run
+    beside it (``window_first_fits`` in ``csrc/window.cu``; ``window_rows`` = sink + recent)
+    costs 5 tiles more: the window split and the merge then follow the INT2 grid, and the
+    merge spreads the many splits of few requests over few CTAs.  Measured on B200, one call:
+    B2 x 128K, 74 splits 62.4 us against 73 splits 47.1; B4 x 64K, 37 splits 56.0 against
+    36 splits 45.8."""
+    tc = {(512, 64, 16), (512, 64, 8), (256, 32, 40), (256, 32, 16)}
     if ctas_per_sm is None:
-        tc = {(512, 64, 16), (512, 64, 8), (256, 32, 40), (256, 32, 16)}
         ctas_per_sm = 1 if (latent_dim, rope_dim, heads) in tc else 2
     tiles = max(1, math.ceil(max_ctx / (2 * PAGE)))
     slots = sm_count * ctas_per_sm
+    rpc = _window_rpc(latent_dim, rope_dim, window_rows)
     best, best_cost = 1, float("inf")
     for s in range(1, min(tiles, 128) + 1):
         tps = math.ceil(tiles / s)
         if tps < 2 and s > 1:
             break
-        cost = math.ceil(batch * s / slots) * (tps + 3)
+        waves = math.ceil(batch * s / slots)
+        cost = waves * (tps + 3)
+        if (latent_dim, rope_dim, heads) in tc and waves == 1 and s + 1 >= 16:
+            free = sm_count - batch * s
+            if not (free >= 1 and free * 2 * rpc >= batch):
+                cost += 5
         if cost < best_cost:
             best, best_cost = s, cost
     return best
