@@ -8,6 +8,14 @@ sized for the largest captured batch.  This reader takes 64-token pages instead,
 launch, ``rolaq_page_table_from_req_to_token``, no host sync: capturable), and
 ``forward_decode`` runs the packed decode for one layer with preallocated scratch.
 Every buffer is allocated in ``__init__``, none per batch or per layer.
+
+The split count follows the batch, as the reference's per-batch
+``forward_metadata.num_kv_splits`` under a ``max_kv_splits`` bound does
+(``deployment/patches/rolaq_sglang.patch:51-72, 98-111``): the
+scratch holds ``max_batch * (num_kv_splits + 1)`` partials per head, and a batch of ``b``
+requests takes ``ops.default_num_splits(b, max_context_len)`` splits within that room, so one
+long request is spread over the SMs instead of the few CTAs ``max_batch``'s count gives it.
+An explicit ``num_kv_splits`` fixes the count for every batch.
 """
 
 from __future__ import annotations
@@ -27,8 +35,10 @@ class PackedMLADecodeBackend:
         self.num_heads = num_heads
         self.sm_scale = float(sm_scale)
         self.max_batch = max_batch
+        self.max_context_len = max_context_len
         self.max_pages = math.ceil(max_context_len / ops.PAGE)
         d, dr = pool.kv_lora_rank, pool.qk_rope_head_dim
+        self.fixed_splits = bool(num_kv_splits)
         self.num_kv_splits = num_kv_splits or ops.default_num_splits(max_batch, max_context_len, latent_dim=d,
                                                                      rope_dim=dr, heads=num_heads)
         dev = pool.device
@@ -39,6 +49,17 @@ class PackedMLADecodeBackend:
         self.attn_lse = torch.empty(max_batch, num_heads, self.num_kv_splits + 1, dtype=torch.float32, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         self.batch = 0
+        self.splits = self.num_kv_splits
+
+    def splits_for(self, batch: int) -> int:
+        """KV splits for a batch of ``batch`` requests: the fixed count, or the default count for
+        ``batch`` x ``max_context_len`` bounded by the partials the scratch holds per request."""
+        if self.fixed_splits or batch <= 0:
+            return self.num_kv_splits
+        room = self.max_batch * (self.num_kv_splits + 1) // batch - 1
+        s = ops.default_num_splits(batch, self.max_context_len, latent_dim=self.pool.kv_lora_rank,
+                                   rope_dim=self.pool.qk_rope_head_dim, heads=self.num_heads)
+        return max(1, min(s, room))
 
     def init_forward_metadata(self, req_to_token: torch.Tensor, req_pool_indices: torch.Tensor,
                               seq_lens: torch.Tensor) -> None:
@@ -54,6 +75,7 @@ class PackedMLADecodeBackend:
         ops.page_table_from_req_to_token(req_to_token, req_pool_indices, seq_lens, self.page_table[:b],
                                          self.seq_lens[:b], err=self.err)
         self.batch = b
+        self.splits = self.splits_for(b)
 
     def forward_decode(self, q: torch.Tensor, layer_id: int, out: torch.Tensor | None = None) -> torch.Tensor:
         """One layer's decode attention: ``q`` ``[B, H * (D + Dr)]`` or ``[B, H, D + Dr]`` (rotated
@@ -61,6 +83,9 @@ class PackedMLADecodeBackend:
         b = self.batch
         d, dr = self.pool.kv_lora_rank, self.pool.qk_rope_head_dim
         q = q.view(b, self.num_heads, d + dr)
+        h, parts = self.num_heads, self.splits + 1
+        logits = self.attn_logits.view(-1)[: b * h * parts * d].view(b, h, parts, d)
+        lse = self.attn_lse.view(-1)[: b * h * parts].view(b, h, parts)
         return packed_mla_decode_gf_fwd(q, self.pool, layer_id, self.page_table[:b], self.seq_lens[:b],
-                                        self.sm_scale, self.num_kv_splits, attn_logits=self.attn_logits[:b],
-                                        attn_lse=self.attn_lse[:b], out=out, err=self.err)
+                                        self.sm_scale, self.splits, attn_logits=logits, attn_lse=lse, out=out,
+                                        err=self.err)

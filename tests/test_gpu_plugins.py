@@ -258,6 +258,42 @@ def test_backend_shim_from_req_to_token():
     assert int(be.page_table[0, 1].item()) == -1 and int(be.page_table[0, 0].item()) == int(pt[0, 0].item())
 
 
+def test_backend_shim_single_long_request_takes_more_splits():
+    """A shim sized for 64 requests decodes a batch of one 12,000-token request on the split
+    count of a one-request batch (64 splits, not max_batch's 2), inside the same scratch, bit
+    for bit as the reader with that count, and within the decode tolerance of the oracle."""
+    from mla_kv_quant_b200.backend import PackedMLADecodeBackend
+
+    d, dr, h, L = 512, 64, 16, 12000
+    n = (L + 63) // 64
+    pool = PackedLatentPool(64 * (n + 2), 1, max_reqs=1, rotations={0: synth.rotation(d, 5)})
+    g = torch.Generator().manual_seed(6)
+    pt = (torch.randperm(n + 1, generator=g)[:n] + 1).to(torch.int32).reshape(1, n).cuda()
+    pos = torch.arange(L, device="cuda")
+    slots = pt[0, pos // 64] * 64 + pos % 64
+    req_to_token = torch.zeros(1, 16384, dtype=torch.int32, device="cuda")
+    req_to_token[0, :L] = slots.int()
+    pool.set_window_meta(False, torch.full((L,), L, dtype=torch.int32, device="cuda"),
+                         torch.zeros(L, dtype=torch.int64, device="cuda"))
+    pool.set_kv_buffer(0, slots.long(), synth.latents(L, d, seed=7, device="cuda"),
+                       synth.normal_bf16((L, dr), seed=8, device="cuda"), positions=pos.int())
+    be = PackedMLADecodeBackend(pool, h, max_batch=64, max_context_len=16384, sm_scale=0.07)
+    req_idx = torch.zeros(1, dtype=torch.int64, device="cuda")
+    seq = torch.tensor([L], dtype=torch.int64, device="cuda")
+    be.init_forward_metadata(req_to_token, req_idx, seq)
+    assert be.num_kv_splits == 2 and be.splits == 64
+    q = synth.normal_bf16((1, h, d + dr), seed=9, device="cuda")
+    got = be.forward_decode(q.view(1, -1), 0)
+    ref = packed_mla_decode_gf_fwd(q, pool, 0, pt, seq.int(), 0.07, 64)
+    torch.cuda.synchronize()
+    assert int(be.err.item()) == 0
+    assert torch.equal(got, ref)
+    want, _ = odecode.decode(_oracle_pool(pool, 0), bits(q), pt.cpu().numpy(), [L], 0.07)
+    o = got.float().cpu().numpy()[0]
+    assert np.max(np.abs(o - want[0]) - np.exp2(np.floor(np.log2(np.maximum(np.abs(want[0]), 1e-30))) - 8)) <= 2e-2
+    assert cosine(o, want[0]) >= 0.9995
+
+
 def test_hf_window_lifecycle_on_gpu(golden_dir):
     """The HF path's s4r16 window on the GPU: a 30-token prefill and 25 decode steps (batch 2,
     the second row left-padded by 3, the pad mask growing with the sequence as HF passes it).

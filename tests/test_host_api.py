@@ -116,6 +116,26 @@ def test_env_flags(monkeypatch):
     assert envs.SGLANG_ROLAQ_MLA_FUSED_DECODE_WRITE.get() is False
 
 
+def test_backend_split_count_follows_the_batch():
+    """The decode-backend shim sizes its scratch for max_batch x (num_kv_splits + 1) partials
+    per head and gives a smaller batch more splits within that room; an explicit
+    num_kv_splits stays fixed."""
+    from types import SimpleNamespace
+
+    from mla_kv_quant_b200.backend import PackedMLADecodeBackend
+
+    pool = SimpleNamespace(kv_lora_rank=512, qk_rope_head_dim=64, device=torch.device("cpu"))
+    be = PackedMLADecodeBackend(pool, 16, max_batch=64, max_context_len=16384, sm_scale=0.07)
+    assert be.num_kv_splits == ops.default_num_splits(64, 16384) == 2
+    assert be.splits_for(64) == 2
+    assert be.splits_for(1) == ops.default_num_splits(1, 16384) == 64
+    for b in range(1, 65):
+        s = be.splits_for(b)
+        assert 1 <= s and b * (s + 1) <= 64 * (2 + 1)
+    fixed = PackedMLADecodeBackend(pool, 16, max_batch=8, max_context_len=1024, sm_scale=0.07, num_kv_splits=3)
+    assert fixed.splits_for(1) == fixed.splits_for(8) == 3
+
+
 def test_split_heuristics_and_ranges():
     s = ops.default_num_splits(64, 16384)
     assert 1 <= s <= 64
