@@ -1,17 +1,20 @@
 """Sequence-split decode of long requests across the GPUs of one node.
 
-Each rank owns one contiguous, page-aligned slice of every request's positions
-(and the cache pages of that slice).  It runs the packed decode kernel restricted
-to its slice (``token_range``) and merges its own splits into one FP32 partial
-``(o, lse)`` per (request, head); the ranks exchange those partials with one NCCL ``all_gather_into_tensor`` of
-``B * H * (D + 4) * 4`` bytes per rank, about 33 KB for one DeepSeek-V2-Lite request.  Every rank then merges the ``world`` partials
-with the same LSE kernel and holds the full output.
+Each rank owns one contiguous, page-aligned slice of every request's positions (and the
+cache pages of that slice).  It runs the packed decode kernel restricted to its slice
+(``token_range``) and merges its own splits into one FP32 partial ``(o, lse)`` per
+(request, head): ``B * H * (D + 4) * 4`` bytes per rank, about 33 KB for one
+DeepSeek-V2-Lite request.  The ranks exchange those partials in one of two ways.
+``PeerExchange`` has the merging kernel store them into every rank's receive buffer over
+NVLink (CUDA IPC mappings) and a bounded wait collect them.  Otherwise one NCCL
+``all_gather_into_tensor`` moves them.  Every rank then merges the ``world`` partials with
+the same LSE kernel and holds the full output.  Without a process group the decoder runs
+on one GPU holding the whole request.
 
-The reference serves one GPU only (``deployment/serve.py:135-136``); this module
-is the multi-GPU extension the packed path's sharding needs.  No kernel reads
-another GPU's memory: the partials cross NVLink through NCCL.
+The reference serves one GPU only (``deployment/serve.py:135-136``); this module is the
+multi-GPU extension the packed path's sharding needs.  No kernel reads another GPU's
+memory: the exchange writes to peers and reads its own receive buffer.
 """
-
 from __future__ import annotations
 
 from typing import Callable
@@ -31,6 +34,10 @@ def rank_token_range(seq_len: int, world: int, rank: int, page: int = ops.PAGE) 
     return start, end
 
 
+def _distributed() -> bool:
+    return dist.is_available() and dist.is_initialized()
+
+
 def gather_merge(o_local: torch.Tensor, lse_local: torch.Tensor, group=None,
                  merge: Callable[[torch.Tensor, torch.Tensor], tuple[torch.Tensor, torch.Tensor]] | None = None):
     """All-gather per-rank partials ``o [rows, D]`` (FP32 or BF16) / ``lse [rows]`` and
@@ -42,13 +49,16 @@ def gather_merge(o_local: torch.Tensor, lse_local: torch.Tensor, group=None,
     ``merge(parts_o [world, rows, D], parts_lse [world, rows]) -> (out, lse)``; the
     default is the CUDA merge kernel (``rolaq_merge_partials``) writing FP32.
     """
-    world = dist.get_world_size(group)
+    world = dist.get_world_size(group) if _distributed() else 1  # no process group: one rank
     rows, d = o_local.shape
     packed = torch.zeros(rows, d + 4, dtype=torch.float32, device=o_local.device)
     packed[:, :d] = o_local  # FP32 or BF16 partials
     packed[:, d] = lse_local
-    flat = torch.empty(world * rows, d + 4, dtype=torch.float32, device=o_local.device)
-    dist.all_gather_into_tensor(flat, packed, group=group)
+    if world > 1:
+        flat = torch.empty(world * rows, d + 4, dtype=torch.float32, device=o_local.device)
+        dist.all_gather_into_tensor(flat, packed, group=group)
+    else:
+        flat = packed
     parts = flat.view(world, rows, d + 4)
     parts_o = parts[:, :, :d]
     parts_lse = parts[:, :, d]
@@ -68,8 +78,8 @@ class SequenceSplitDecoder:
         peer memory; without one they go through one NCCL all-gather."""
         self.pool = pool
         self.group = group
-        self.world = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group) if _distributed() else 1  # no process group: one GPU
+        self.rank = dist.get_rank(group) if _distributed() else 0
         self.exchange = exchange
 
     def local_partial(self, q, layer_id, page_table, seq_lens, sm_scale, num_splits, token_range):
@@ -89,11 +99,18 @@ class SequenceSplitDecoder:
                            out_lse=lse)
         return o, lse
 
-    def decode(self, q, layer_id, page_table, seq_lens_host: list[int], seq_lens, sm_scale, num_splits=4):
-        """``q [B, H, D + Dr]`` -> ``out [B, H, D]`` BF16 on every rank."""
+    def decode(self, q, layer_id, page_table, seq_lens_host: list[int], seq_lens, sm_scale,
+               num_splits: int | None = None):
+        """``q [B, H, D + Dr]`` -> ``out [B, H, D]`` BF16 on every rank.  ``num_splits`` (INT2
+        splits per request of this rank's slice) defaults to ``ops.default_num_splits`` for
+        the batch and the longest slice of this rank."""
         b, h, _ = q.shape
-        rng = torch.tensor([rank_token_range(int(L), self.world, self.rank) for L in seq_lens_host],
-                           dtype=torch.int32, device=q.device)
+        ranges = [rank_token_range(int(L), self.world, self.rank) for L in seq_lens_host]
+        if num_splits is None:
+            longest = max([e - s for s, e in ranges] + [1])
+            num_splits = ops.default_num_splits(b, longest, latent_dim=self.pool.kv_lora_rank,
+                                                rope_dim=self.pool.qk_rope_head_dim, heads=h)
+        rng = torch.tensor(ranges, dtype=torch.int32, device=q.device)
         if self.exchange is not None:
             d = self.pool.kv_lora_rank
             part_o = torch.empty(b, h, num_splits + 1, d, dtype=torch.float32, device=q.device)

@@ -114,3 +114,40 @@ def test_peer_wait_gives_up_when_no_rank_pushes():
     finally:
         xch.state[0] = 0
         xch.close()
+
+
+def test_sequence_split_decoder_on_one_gpu():
+    """``SequenceSplitDecoder`` without a process group (one GPU holds the whole request),
+    through both exchanges, on the default split count of its slice: the two outputs are
+    identical and equal the merged decode call's within BF16 rounding of its weights."""
+    from mla_kv_quant_b200.mla_packed_decode import packed_mla_decode_gf_fwd
+    from mla_kv_quant_b200.pool import PackedLatentPool
+    from mla_kv_quant_b200.seqsplit import SequenceSplitDecoder
+
+    d, dr, h, L = 512, 64, 16, 12000
+    n = (L + 63) // 64
+    pool = PackedLatentPool(64 * (n + 2), 1, max_reqs=1, rotations={0: synth.rotation(d, 11)})
+    g = torch.Generator().manual_seed(12)
+    pt = (torch.randperm(n + 1, generator=g)[:n] + 1).to(torch.int32).reshape(1, n).cuda()
+    pos = torch.arange(L, device="cuda")
+    slots = pt[0, pos // 64] * 64 + pos % 64
+    pool.set_window_meta(False, torch.full((L,), L, dtype=torch.int32, device="cuda"),
+                         torch.zeros(L, dtype=torch.int64, device="cuda"))
+    pool.set_kv_buffer(0, slots.long(), synth.latents(L, d, seed=13, device="cuda"),
+                       synth.normal_bf16((L, dr), seed=14, device="cuda"), positions=pos.int())
+    q = synth.normal_bf16((1, h, d + dr), seed=15, device="cuda")
+    sl = torch.tensor([L], dtype=torch.int32, device="cuda")
+    splits = ops.default_num_splits(1, L)
+    assert splits + 1 >= 16  # the slice's splits take the many-partials merge
+    out_nccl = SequenceSplitDecoder(pool).decode(q, 0, pt, [L], sl, 0.07)
+    xch = PeerExchange(h, d)
+    try:
+        out_peer = SequenceSplitDecoder(pool, exchange=xch).decode(q, 0, pt, [L], sl, 0.07)
+        torch.cuda.synchronize()
+    finally:
+        xch.close()
+    ref = packed_mla_decode_gf_fwd(q, pool, 0, pt, sl, 0.07, splits)
+    torch.cuda.synchronize()
+    assert torch.equal(out_peer, out_nccl)
+    diff = (out_peer.float() - ref.float()).abs()
+    assert float(diff.max()) <= 2 ** -8 * float(ref.float().abs().max()), float(diff.max())
