@@ -9,7 +9,7 @@
 // allocation per rank), and the final merge waits for every rank's partial:
 //
 //   merge_push_kernel  (rank r: its splits -> (o, lse) in FP32 -> recv[q][parity][r] for every q,
-//                       then, by the grid's last CTA, flags_q[r] = step with release semantics)
+//                       then, by the grid's last CTA, flags_q[r] = step after a system fence)
 //   wait_merge_kernel  (rank q: waits, bounded, until flags_q[r] >= step for every r, then merges
 //                       recv[q][parity][0 .. world) -> BF16 / FP32 out)
 //
@@ -26,8 +26,8 @@ namespace peer {
 
 constexpr int kRowsPerCta = 4;
 
-__device__ __forceinline__ void st_release_sys(int32_t* p, int32_t v) {
-  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(int32_t* p, int32_t v) {
+  asm volatile("st.relaxed.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ int32_t ld_acquire_sys(const int32_t* p) {
   int32_t v;
@@ -135,8 +135,11 @@ __global__ void __launch_bounds__(WIDE ? wide::kThreads : kRowsPerCta * D / 8)
   }
   // The CTA's stores are ordered before its count by the barrier and a GPU-scope fence (every
   // CTA of the grid is on this GPU); the last CTA to count acquires them all and makes them
-  // visible system-wide with one fence before it releases the flags.  Release and acquire
-  // are cumulative, so a peer that acquires a flag sees every CTA's stores.
+  // visible system-wide with one fence before it writes the flags.  That fence and each
+  // flag store after it form a release pattern (a fence, then a strong store), and release
+  // and acquire are cumulative, so a peer that acquires a flag sees every CTA's stores.  The
+  // flag stores are relaxed: a release store would fence again, waiting for the previous
+  // flag's NVLink round trip, so the world's flags would go out one round trip apart.
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
@@ -145,7 +148,7 @@ __global__ void __launch_bounds__(WIDE ? wide::kThreads : kRowsPerCta * D / 8)
       __threadfence_system();
       for (int q = 0; q < world; ++q) {
         int32_t* flags = reinterpret_cast<int32_t*>(reinterpret_cast<float*>(peers[q]) + 2 * world * slot);
-        st_release_sys(flags + rank, step);
+        st_relaxed_sys(flags + rank, step);
       }
       state[1] = 0;
       state[0] = step;
