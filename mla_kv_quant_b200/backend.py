@@ -39,8 +39,11 @@ class PackedMLADecodeBackend:
         self.max_pages = math.ceil(max_context_len / ops.PAGE)
         d, dr = pool.kv_lora_rank, pool.qk_rope_head_dim
         self.fixed_splits = bool(num_kv_splits)
+        # sink + recent BF16 window rows of the pool (s4r16 unless it says otherwise)
+        self.window_rows = getattr(pool, "_win_p", 4) + getattr(pool, "_win_r", 16)
         self.num_kv_splits = num_kv_splits or ops.default_num_splits(max_batch, max_context_len, latent_dim=d,
-                                                                     rope_dim=dr, heads=num_heads)
+                                                                     rope_dim=dr, heads=num_heads,
+                                                                     window_rows=self.window_rows)
         dev = pool.device
         self.page_table = torch.full((max_batch, self.max_pages), -1, dtype=torch.int32, device=dev)
         self.seq_lens = torch.zeros(max_batch, dtype=torch.int32, device=dev)
@@ -58,7 +61,8 @@ class PackedMLADecodeBackend:
             return self.num_kv_splits
         room = self.max_batch * (self.num_kv_splits + 1) // batch - 1
         s = ops.default_num_splits(batch, self.max_context_len, latent_dim=self.pool.kv_lora_rank,
-                                   rope_dim=self.pool.qk_rope_head_dim, heads=self.num_heads)
+                                   rope_dim=self.pool.qk_rope_head_dim, heads=self.num_heads,
+                                   window_rows=self.window_rows)
         return max(1, min(s, room))
 
     def init_forward_metadata(self, req_to_token: torch.Tensor, req_pool_indices: torch.Tensor,

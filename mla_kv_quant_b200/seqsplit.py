@@ -109,7 +109,9 @@ class SequenceSplitDecoder:
         if num_splits is None:
             longest = max([e - s for s, e in ranges] + [1])
             num_splits = ops.default_num_splits(b, longest, latent_dim=self.pool.kv_lora_rank,
-                                                rope_dim=self.pool.qk_rope_head_dim, heads=h)
+                                                rope_dim=self.pool.qk_rope_head_dim, heads=h,
+                                                window_rows=getattr(self.pool, "_win_p", 4)
+                                                + getattr(self.pool, "_win_r", 16))
         rng = torch.tensor(ranges, dtype=torch.int32, device=q.device)
         if self.exchange is not None:
             d = self.pool.kv_lora_rank
